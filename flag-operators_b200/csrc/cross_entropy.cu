@@ -1,0 +1,595 @@
+// Fused cross-entropy (forward, backward, vocabulary-sharded pieces) for sm_100a.
+//
+// Semantics follow the reference CPU branch, F.cross_entropy
+// (operators/fused_cross_entropy.py:327-331), including label smoothing:
+//   loss_b = lse_b - (1 - e) x[b, t_b] - e * mean_j x[b, j]   (0 when t_b == ignore_index)
+//   dloss/dx[b, j] = scale_b * (softmax_j - (1 - e)[j == t_b] - e / V)
+// with scale_b = dout (* 1/n_valid for 'mean').  'mean' over zero valid rows is
+// 0/0 = NaN, as torch.
+//
+// Design: one CTA per row (grid-stride persistent).  Pass 1 streams the row once
+// with 16-byte loads and keeps an online (max, sum exp) pair per thread, merged
+// by a block reduction.  When the gradient is wanted in the same call, pass 2
+// re-reads the row — pass 1 loaded it with an L2 evict_last policy so the second
+// read is served from L2 — and writes dlogits, so forward+backward costs one
+// HBM read and one HBM write of B x V.  exp is exp2 with a pre-scaled argument
+// (one FFMA + one MUFU.EX2 per element).
+#include <math.h>
+
+#include "common.cuh"
+
+namespace fo {
+namespace {
+
+constexpr int kThreads = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+struct MS {
+  float m;  // running max
+  float s;  // sum of exp(x - m)
+};
+
+__device__ __forceinline__ MS ms_merge(MS a, MS b) {
+  const float m = fmaxf(a.m, b.m);
+  if (m == -INFINITY) return {m, 0.f};
+  return {m, a.s * fast_exp2((a.m - m) * kLog2e) + b.s * fast_exp2((b.m - m) * kLog2e)};
+}
+
+template <int E>
+__device__ __forceinline__ void ms_add_vec(MS& st, float& rsum, const float* f, bool ls) {
+  float lm = f[0];
+#pragma unroll
+  for (int i = 1; i < E; ++i) lm = fmaxf(lm, f[i]);
+  if (lm > st.m) {
+    st.s = (st.m == -INFINITY) ? 0.f : st.s * fast_exp2((st.m - lm) * kLog2e);
+    st.m = lm;
+  }
+  if (st.m != -INFINITY) {
+    const float mb = st.m * kLog2e;
+#pragma unroll
+    for (int i = 0; i < E; ++i) st.s += fast_exp2(fmaf(f[i], kLog2e, -mb));
+  }
+  if (ls) {
+#pragma unroll
+    for (int i = 0; i < E; ++i) rsum += f[i];
+  }
+}
+
+__device__ __forceinline__ void ms_add_scalar(MS& st, float& rsum, float f, bool ls) {
+  if (f > st.m) {
+    st.s = (st.m == -INFINITY) ? 0.f : st.s * fast_exp2((st.m - f) * kLog2e);
+    st.m = f;
+  }
+  if (st.m != -INFINITY) st.s += fast_exp2((f - st.m) * kLog2e);
+  if (ls) rsum += f;
+}
+
+// Block-wide merge of (m, s) and of the row sum; result valid in every thread.
+__device__ __forceinline__ void block_ms(MS& st, float& rsum, float* sm) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    MS other{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o)};
+    st = ms_merge(st, other);
+    rsum += __shfl_xor_sync(0xffffffffu, rsum, o);
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    sm[wid] = st.m;
+    sm[32 + wid] = st.s;
+    sm[64 + wid] = rsum;
+  }
+  __syncthreads();
+  MS t{lane < nw ? sm[lane] : -INFINITY, lane < nw ? sm[32 + lane] : 0.f};
+  float r = lane < nw ? sm[64 + lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    MS other{__shfl_xor_sync(0xffffffffu, t.m, o), __shfl_xor_sync(0xffffffffu, t.s, o)};
+    t = ms_merge(t, other);
+    r += __shfl_xor_sync(0xffffffffu, r, o);
+  }
+  st = t;
+  rsum = r;
+}
+
+// Statistics of n contiguous elements starting at p (any alignment).
+template <typename T>
+__device__ __forceinline__ void row_stats(const T* __restrict__ p, int64_t n, bool ls,
+                                          bool keep_in_l2, MS& st, float& rsum) {
+  constexpr int E = Vec16<T>::E;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(p);
+  int64_t head = (int64_t)(((16 - (addr & 15)) & 15) / sizeof(T));
+  if ((addr % sizeof(T)) != 0) head = n;  // not even element-aligned: scalar only
+  if (head > n) head = n;
+  for (int64_t j = threadIdx.x; j < head; j += blockDim.x) ms_add_scalar(st, rsum, to_f<T>(p[j]), ls);
+  const T* pv = p + head;
+  const int64_t nvec = (n - head) / E;
+  const uint64_t pol = keep_in_l2 ? l2_policy_evict_last() : l2_policy_evict_first();
+  int64_t v = threadIdx.x;
+  // 4 independent 16-byte loads in flight per thread
+  for (; v + 3 * blockDim.x < nvec; v += 4 * blockDim.x) {
+    uint4 r[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) r[u] = ld_global_hint_v4(pv + (v + u * blockDim.x) * E, pol);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float f[E];
+      unpack16<T>(r[u], f);
+      ms_add_vec<E>(st, rsum, f, ls);
+    }
+  }
+  for (; v < nvec; v += blockDim.x) {
+    float f[E];
+    unpack16<T>(ld_global_hint_v4(pv + v * E, pol), f);
+    ms_add_vec<E>(st, rsum, f, ls);
+  }
+  for (int64_t j = head + nvec * E + threadIdx.x; j < n; j += blockDim.x)
+    ms_add_scalar(st, rsum, to_f<T>(p[j]), ls);
+}
+
+// Writes g[j] = scale * (exp(x[j] - lse) - eps_v - (1-e)[j + col0 == t]) for j < n.
+// scale == 0 (ignored row) writes zeros without reading x.
+template <typename T>
+__device__ __forceinline__ void row_grad(const T* __restrict__ p, T* __restrict__ g, int64_t n,
+                                         int64_t col0, int64_t t, float lse, float scale,
+                                         float eps_v, float one_m_e) {
+  constexpr int E = Vec16<T>::E;
+  const float lb = lse * kLog2e;
+  const float se = scale * eps_v;
+  const uintptr_t ap = reinterpret_cast<uintptr_t>(p), ag = reinterpret_cast<uintptr_t>(g);
+  const bool vec = ((ap & 15) == (ag & 15)) && (ap % sizeof(T)) == 0;
+  int64_t head = vec ? (int64_t)(((16 - (ap & 15)) & 15) / sizeof(T)) : n;
+  if (head > n) head = n;
+  auto one = [&](int64_t j, float x) -> float {
+    float v = (scale == 0.f) ? 0.f : scale * fast_exp2(fmaf(x, kLog2e, -lb)) - se;
+    if (j + col0 == t) v -= scale * one_m_e;
+    return v;
+  };
+  for (int64_t j = threadIdx.x; j < head; j += blockDim.x)
+    g[j] = from_f<T>(one(j, scale == 0.f ? 0.f : to_f<T>(p[j])));
+  const int64_t nvec = (n - head) / E;
+  const T* pv = p + head;
+  T* gv = g + head;
+  const uint64_t pol = l2_policy_evict_first();
+  int64_t v = threadIdx.x;
+  for (; v + 3 * blockDim.x < nvec; v += 4 * blockDim.x) {
+    uint4 r[4];
+    if (scale != 0.f) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) r[u] = ld_global_hint_v4(pv + (v + u * blockDim.x) * E, pol);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float f[E];
+      if (scale != 0.f) unpack16<T>(r[u], f);
+      const int64_t j0 = head + (v + u * blockDim.x) * E;
+#pragma unroll
+      for (int i = 0; i < E; ++i) f[i] = one(j0 + i, scale != 0.f ? f[i] : 0.f);
+      st_global_stream_v4(gv + (v + u * blockDim.x) * E, pack16<T>(f));
+    }
+  }
+  for (; v < nvec; v += blockDim.x) {
+    float f[E];
+    if (scale != 0.f) unpack16<T>(ld_global_hint_v4(pv + v * E, pol), f);
+    const int64_t j0 = head + v * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) f[i] = one(j0 + i, scale != 0.f ? f[i] : 0.f);
+    st_global_stream_v4(gv + v * E, pack16<T>(f));
+  }
+  for (int64_t j = head + nvec * E + threadIdx.x; j < n; j += blockDim.x)
+    g[j] = from_f<T>(one(j, scale == 0.f ? 0.f : to_f<T>(p[j])));
+}
+
+// n_valid = #(target != ignore_index), written as float.
+__global__ void ce_count_valid_kernel(const int64_t* __restrict__ target, int64_t B,
+                                      int64_t ignore_index, float* __restrict__ n_valid) {
+  __shared__ float red[32];
+  float c = 0.f;
+  for (int64_t b = threadIdx.x; b < B; b += blockDim.x) c += (target[b] != ignore_index) ? 1.f : 0.f;
+  c = block_sum(c, red);
+  if (threadIdx.x == 0) *n_valid = c;
+}
+
+__device__ __forceinline__ float read_scalar(const void* p, int dt, int64_t i) {
+  switch (dt) {
+    case FO_F32: return reinterpret_cast<const float*>(p)[i];
+    case FO_F16: return __half2float(reinterpret_cast<const __half*>(p)[i]);
+    case FO_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    case FO_F64: return (float)reinterpret_cast<const double*>(p)[i];
+  }
+  return 0.f;
+}
+
+template <typename T, bool LS>
+__global__ void __launch_bounds__(kThreads)
+ce_fwd_kernel(const T* __restrict__ logits, const int64_t* __restrict__ target,
+              float* __restrict__ loss_rows, float* __restrict__ lse_out, T* __restrict__ dlogits,
+              const float* __restrict__ n_valid, int64_t B, int64_t V, int64_t ld,
+              int64_t ignore_index, float eps, int reduction) {
+  __shared__ float sm[96];
+  __shared__ float s_lse;
+  const bool grad = dlogits != nullptr;
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const T* row = logits + b * ld;
+    const int64_t t = target[b];
+    const bool valid = (t != ignore_index);
+    MS st{-INFINITY, 0.f};
+    float rsum = 0.f;
+    row_stats<T>(row, V, LS, grad, st, rsum);
+    block_ms(st, rsum, sm);
+    if (threadIdx.x == 0) {
+      const float lse = st.m + logf(st.s);
+      float loss = 0.f;
+      if (valid) {
+        const float xt = (t >= 0 && t < V) ? to_f<T>(row[t]) : NAN;
+        loss = lse - (1.f - eps) * xt;
+        if (LS) loss -= eps * (rsum / (float)V);
+      }
+      loss_rows[b] = loss;
+      lse_out[b] = lse;
+      s_lse = lse;
+    }
+    if (grad) {
+      __syncthreads();
+      const float lse = s_lse;
+      float scale = valid ? 1.f : 0.f;
+      if (valid && reduction == FO_RED_MEAN) scale = 1.f / *n_valid;
+      row_grad<T>(row, dlogits + b * V, V, 0, t, lse, scale, LS ? eps / (float)V : 0.f,
+                  1.f - eps);
+    }
+  }
+}
+
+// Deterministic single-CTA reduction of loss_rows -> out_scalar (sum or mean).
+__global__ void ce_reduce_kernel(const float* __restrict__ loss_rows, int64_t B,
+                                 const float* __restrict__ n_valid, int reduction,
+                                 float* __restrict__ out_scalar) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int64_t b = threadIdx.x; b < B; b += blockDim.x) s += loss_rows[b];
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) *out_scalar = (reduction == FO_RED_MEAN) ? s / *n_valid : s;
+}
+
+template <typename T, bool LS>
+__global__ void __launch_bounds__(kThreads)
+ce_bwd_kernel(const T* __restrict__ logits, const int64_t* __restrict__ target,
+              const float* __restrict__ lse, const void* __restrict__ dout, int dout_dtype,
+              int dout_is_vector, const float* __restrict__ n_valid, T* __restrict__ dlogits,
+              int64_t B, int64_t Vn, int64_t ld, int64_t col0, int64_t V, int64_t ignore_index,
+              float eps, int reduction) {
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const int64_t t = target[b];
+    const bool valid = (t != ignore_index);
+    float scale = 0.f;
+    if (valid) {
+      scale = read_scalar(dout, dout_dtype, dout_is_vector ? b : 0);
+      if (reduction == FO_RED_MEAN) scale /= *n_valid;
+    }
+    row_grad<T>(logits + b * ld, dlogits + b * Vn, Vn, col0, t, lse[b], scale,
+                LS ? eps / (float)V : 0.f, 1.f - eps);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+ce_scale_kernel(T* __restrict__ g, const void* __restrict__ dout, int dout_dtype, int is_vec,
+                int64_t B, int64_t V, int64_t ld) {
+  if (!is_vec) {
+    const float d = read_scalar(dout, dout_dtype, 0);
+    if (d == 1.0f) return;  // backward of loss.backward(): nothing to scale
+  }
+  constexpr int E = Vec16<T>::E;
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const float d = read_scalar(dout, dout_dtype, is_vec ? b : 0);
+    T* row = g + b * ld;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(row);
+    int64_t head = (a % sizeof(T)) ? V : (int64_t)(((16 - (a & 15)) & 15) / sizeof(T));
+    if (head > V) head = V;
+    for (int64_t j = threadIdx.x; j < head; j += blockDim.x) row[j] = from_f<T>(to_f<T>(row[j]) * d);
+    const int64_t nvec = (V - head) / E;
+    T* rv = row + head;
+    for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+      float f[E];
+      unpack16<T>(ld_global_stream_v4(rv + v * E), f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) f[i] *= d;
+      st_global_stream_v4(rv + v * E, pack16<T>(f));
+    }
+    for (int64_t j = head + nvec * E + threadIdx.x; j < V; j += blockDim.x)
+      row[j] = from_f<T>(to_f<T>(row[j]) * d);
+  }
+}
+
+// Vocabulary shard: per-row (max, sumexp, target logit or 0, row sum).
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+ce_shard_stats_kernel(const T* __restrict__ logits, const int64_t* __restrict__ target,
+                      float* __restrict__ stats, int64_t B, int64_t Vn, int64_t ld, int64_t col0,
+                      int64_t ignore_index) {
+  __shared__ float sm[96];
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const T* row = logits + b * ld;
+    MS st{-INFINITY, 0.f};
+    float rsum = 0.f;
+    row_stats<T>(row, Vn, true, false, st, rsum);
+    block_ms(st, rsum, sm);
+    if (threadIdx.x == 0) {
+      const int64_t t = target[b];
+      float xt = 0.f;
+      if (t != ignore_index && t >= col0 && t < col0 + Vn) xt = to_f<T>(row[t - col0]);
+      stats[b * 4 + 0] = st.m;
+      stats[b * 4 + 1] = st.s;
+      stats[b * 4 + 2] = xt;
+      stats[b * 4 + 3] = rsum;
+    }
+  }
+}
+
+__global__ void ce_shard_combine_kernel(const float* __restrict__ all, int P,
+                                        const int64_t* __restrict__ target,
+                                        float* __restrict__ loss_rows, float* __restrict__ lse_out,
+                                        int64_t B, int64_t V, int64_t ignore_index, float eps) {
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    MS st{-INFINITY, 0.f};
+    float xt = 0.f, rsum = 0.f;
+    for (int p = 0; p < P; ++p) {
+      const float* s = all + ((int64_t)p * B + b) * 4;
+      st = ms_merge(st, MS{s[0], s[1]});
+      xt += s[2];
+      rsum += s[3];
+    }
+    const float lse = st.m + logf(st.s);
+    const int64_t t = target[b];
+    float loss = 0.f;
+    if (t != ignore_index) {
+      loss = (t >= 0 && t < V) ? lse - (1.f - eps) * xt : NAN;
+      if (eps != 0.f) loss -= eps * (rsum / (float)V);
+    }
+    loss_rows[b] = loss;
+    lse_out[b] = lse;
+  }
+}
+
+int grid_rows(int64_t B, int per_sm) {
+  int64_t g = (int64_t)num_sms() * per_sm;
+  return (int)(g < B ? g : B);
+}
+
+template <typename T>
+int ce_fwd_t(const void* logits, const int64_t* target, float* loss_rows, float* lse,
+             float* out_scalar, float* n_valid, void* dlogits, int64_t B, int64_t V, int64_t ld,
+             int64_t ignore_index, float eps, int reduction, cudaStream_t st) {
+  ce_count_valid_kernel<<<1, 1024, 0, st>>>(target, B, ignore_index, n_valid);
+  if (int rc = check_launch("ce_count_valid_kernel")) return rc;
+  const int grid = grid_rows(B, 4);
+  if (eps != 0.f)
+    ce_fwd_kernel<T, true><<<grid, kThreads, 0, st>>>((const T*)logits, target, loss_rows, lse,
+                                                      (T*)dlogits, n_valid, B, V, ld,
+                                                      ignore_index, eps, reduction);
+  else
+    ce_fwd_kernel<T, false><<<grid, kThreads, 0, st>>>((const T*)logits, target, loss_rows, lse,
+                                                       (T*)dlogits, n_valid, B, V, ld,
+                                                       ignore_index, eps, reduction);
+  if (int rc = check_launch("ce_fwd_kernel")) return rc;
+  if (reduction != FO_RED_NONE) {
+    ce_reduce_kernel<<<1, 1024, 0, st>>>(loss_rows, B, n_valid, reduction, out_scalar);
+    return check_launch("ce_reduce_kernel");
+  }
+  return FO_OK;
+}
+
+template <typename T>
+int ce_bwd_t(const void* logits, const int64_t* target, const float* lse, const void* dout,
+             int dout_dtype, int dout_is_vector, const float* n_valid, void* dlogits, int64_t B,
+             int64_t Vn, int64_t ld, int64_t col0, int64_t V, int64_t ignore_index, float eps,
+             int reduction, cudaStream_t st) {
+  const int grid = grid_rows(B, 4);
+  if (eps != 0.f)
+    ce_bwd_kernel<T, true><<<grid, kThreads, 0, st>>>(
+        (const T*)logits, target, lse, dout, dout_dtype, dout_is_vector, n_valid, (T*)dlogits, B,
+        Vn, ld, col0, V, ignore_index, eps, reduction);
+  else
+    ce_bwd_kernel<T, false><<<grid, kThreads, 0, st>>>(
+        (const T*)logits, target, lse, dout, dout_dtype, dout_is_vector, n_valid, (T*)dlogits, B,
+        Vn, ld, col0, V, ignore_index, eps, reduction);
+  return check_launch("ce_bwd_kernel");
+}
+
+int check_common(const void* logits, const void* target, int64_t B, int64_t V, int64_t ld,
+                 int dtype, const char* op) {
+  FO_CHECK_ARG(B >= 0 && V > 0 && ld >= V, "%s: bad shape B=%lld V=%lld ld=%lld", op,
+               (long long)B, (long long)V, (long long)ld);
+  FO_CHECK_ARG(B == 0 || (logits && target), "%s: null pointer", op);
+  if (dtype != FO_F32 && dtype != FO_F16 && dtype != FO_BF16) {
+    set_error("%s: unsupported logits dtype code %d", op, dtype);
+    return FO_EDTYPE;
+  }
+  return FO_OK;
+}
+
+}  // namespace
+}  // namespace fo
+
+using namespace fo;
+
+extern "C" int fo_ce_workspace_bytes(int64_t B, int64_t* bytes) {
+  clear_error();
+  FO_CHECK_ARG(bytes && B >= 0, "fo_ce_workspace_bytes: bad argument");
+  *bytes = 0;
+  return FO_OK;
+}
+
+extern "C" int fo_ce_fwd(const void* logits, const int64_t* target, float* loss_rows, float* lse,
+                         float* out_scalar, float* n_valid_out, void* dlogits, int64_t B,
+                         int64_t V, int64_t ld, int64_t ignore_index, float label_smoothing,
+                         int reduction, int dtype, void* workspace, int64_t ws_bytes,
+                         void* stream) {
+  (void)workspace;
+  (void)ws_bytes;
+  clear_error();
+  if (int rc = check_common(logits, target, B, V, ld, dtype, "fo_ce_fwd")) return rc;
+  FO_CHECK_ARG(reduction >= FO_RED_NONE && reduction <= FO_RED_SUM, "fo_ce_fwd: bad reduction %d",
+               reduction);
+  FO_CHECK_ARG(loss_rows && lse && n_valid_out, "fo_ce_fwd: null output pointer");
+  FO_CHECK_ARG(reduction == FO_RED_NONE || out_scalar, "fo_ce_fwd: null out_scalar");
+  FO_CHECK_ARG(label_smoothing >= 0.f && label_smoothing <= 1.f, "fo_ce_fwd: bad label_smoothing");
+  cudaStream_t st = as_stream(stream);
+  if (B == 0) {
+    cudaMemsetAsync(n_valid_out, 0, sizeof(float), st);
+    if (reduction != FO_RED_NONE) {
+      ce_reduce_kernel<<<1, 32, 0, st>>>(loss_rows, 0, n_valid_out, reduction, out_scalar);
+      return check_launch("ce_reduce_kernel");
+    }
+    return FO_OK;
+  }
+  switch (dtype) {
+    case FO_F32:
+      return ce_fwd_t<float>(logits, target, loss_rows, lse, out_scalar, n_valid_out, dlogits, B,
+                             V, ld, ignore_index, label_smoothing, reduction, st);
+    case FO_F16:
+      return ce_fwd_t<__half>(logits, target, loss_rows, lse, out_scalar, n_valid_out, dlogits,
+                              B, V, ld, ignore_index, label_smoothing, reduction, st);
+    default:
+      return ce_fwd_t<__nv_bfloat16>(logits, target, loss_rows, lse, out_scalar, n_valid_out,
+                                     dlogits, B, V, ld, ignore_index, label_smoothing, reduction,
+                                     st);
+  }
+}
+
+extern "C" int fo_ce_bwd(const void* logits, const int64_t* target, const float* lse,
+                         const void* dout, int dout_dtype, int dout_is_vector,
+                         const float* n_valid, void* dlogits, int64_t B, int64_t V, int64_t ld,
+                         int64_t ignore_index, float label_smoothing, int reduction, int dtype,
+                         void* stream) {
+  clear_error();
+  if (int rc = check_common(logits, target, B, V, ld, dtype, "fo_ce_bwd")) return rc;
+  if (B == 0) return FO_OK;
+  FO_CHECK_ARG(lse && dout && dlogits && (reduction != FO_RED_MEAN || n_valid),
+               "fo_ce_bwd: null pointer");
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case FO_F32:
+      return ce_bwd_t<float>(logits, target, lse, dout, dout_dtype, dout_is_vector, n_valid,
+                             dlogits, B, V, ld, 0, V, ignore_index, label_smoothing, reduction, st);
+    case FO_F16:
+      return ce_bwd_t<__half>(logits, target, lse, dout, dout_dtype, dout_is_vector, n_valid,
+                              dlogits, B, V, ld, 0, V, ignore_index, label_smoothing, reduction,
+                              st);
+    default:
+      return ce_bwd_t<__nv_bfloat16>(logits, target, lse, dout, dout_dtype, dout_is_vector,
+                                     n_valid, dlogits, B, V, ld, 0, V, ignore_index,
+                                     label_smoothing, reduction, st);
+  }
+}
+
+extern "C" int fo_ce_scale_grad(void* dlogits, const void* dout, int dout_dtype,
+                                int dout_is_vector, int64_t B, int64_t V, int64_t ld, int dtype,
+                                void* stream) {
+  clear_error();
+  FO_CHECK_ARG(B >= 0 && V > 0 && ld >= V, "fo_ce_scale_grad: bad shape");
+  if (B == 0) return FO_OK;
+  FO_CHECK_ARG(dlogits && dout, "fo_ce_scale_grad: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const int grid = grid_rows(B, 4);
+  switch (dtype) {
+    case FO_F32:
+      ce_scale_kernel<float><<<grid, kThreads, 0, st>>>((float*)dlogits, dout, dout_dtype,
+                                                        dout_is_vector, B, V, ld);
+      break;
+    case FO_F16:
+      ce_scale_kernel<__half><<<grid, kThreads, 0, st>>>((__half*)dlogits, dout, dout_dtype,
+                                                         dout_is_vector, B, V, ld);
+      break;
+    case FO_BF16:
+      ce_scale_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(
+          (__nv_bfloat16*)dlogits, dout, dout_dtype, dout_is_vector, B, V, ld);
+      break;
+    default:
+      set_error("fo_ce_scale_grad: unsupported dtype %d", dtype);
+      return FO_EDTYPE;
+  }
+  return check_launch("ce_scale_kernel");
+}
+
+extern "C" int fo_ce_shard_stats(const void* logits, const int64_t* target, float* stats,
+                                 int64_t B, int64_t V_local, int64_t ld, int64_t v_offset,
+                                 int64_t ignore_index, int dtype, void* stream) {
+  clear_error();
+  if (int rc = check_common(logits, target, B, V_local, ld, dtype, "fo_ce_shard_stats")) return rc;
+  if (B == 0) return FO_OK;
+  FO_CHECK_ARG(stats, "fo_ce_shard_stats: null stats");
+  cudaStream_t st = as_stream(stream);
+  const int grid = grid_rows(B, 4);
+  switch (dtype) {
+    case FO_F32:
+      ce_shard_stats_kernel<float><<<grid, kThreads, 0, st>>>((const float*)logits, target, stats,
+                                                              B, V_local, ld, v_offset,
+                                                              ignore_index);
+      break;
+    case FO_F16:
+      ce_shard_stats_kernel<__half><<<grid, kThreads, 0, st>>>(
+          (const __half*)logits, target, stats, B, V_local, ld, v_offset, ignore_index);
+      break;
+    default:
+      ce_shard_stats_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(
+          (const __nv_bfloat16*)logits, target, stats, B, V_local, ld, v_offset, ignore_index);
+  }
+  return check_launch("ce_shard_stats_kernel");
+}
+
+extern "C" int fo_ce_shard_combine(const float* all_stats, int P, const int64_t* target,
+                                   float* loss_rows, float* lse, float* out_scalar,
+                                   float* n_valid_out, int64_t B, int64_t V, int64_t ignore_index,
+                                   float label_smoothing, int reduction, void* stream) {
+  clear_error();
+  FO_CHECK_ARG(P >= 1 && B >= 0 && V > 0, "fo_ce_shard_combine: bad argument");
+  FO_CHECK_ARG(loss_rows && lse && n_valid_out, "fo_ce_shard_combine: null pointer");
+  cudaStream_t st = as_stream(stream);
+  ce_count_valid_kernel<<<1, 1024, 0, st>>>(target, B, ignore_index, n_valid_out);
+  if (int rc = check_launch("ce_count_valid_kernel")) return rc;
+  if (B > 0) {
+    const int grid = (int)((B + 255) / 256);
+    ce_shard_combine_kernel<<<grid, 256, 0, st>>>(all_stats, P, target, loss_rows, lse, B, V,
+                                                  ignore_index, label_smoothing);
+    if (int rc = check_launch("ce_shard_combine_kernel")) return rc;
+  }
+  if (reduction != FO_RED_NONE) {
+    FO_CHECK_ARG(out_scalar, "fo_ce_shard_combine: null out_scalar");
+    ce_reduce_kernel<<<1, 1024, 0, st>>>(loss_rows, B, n_valid_out, reduction, out_scalar);
+    return check_launch("ce_reduce_kernel");
+  }
+  return FO_OK;
+}
+
+extern "C" int fo_ce_shard_bwd(const void* logits, const int64_t* target, const float* lse,
+                               const void* dout, int dout_dtype, int dout_is_vector,
+                               const float* n_valid, void* dlogits, int64_t B, int64_t V_local,
+                               int64_t ld, int64_t v_offset, int64_t V, int64_t ignore_index,
+                               float label_smoothing, int reduction, int dtype, void* stream) {
+  clear_error();
+  if (int rc = check_common(logits, target, B, V_local, ld, dtype, "fo_ce_shard_bwd")) return rc;
+  if (B == 0) return FO_OK;
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case FO_F32:
+      return ce_bwd_t<float>(logits, target, lse, dout, dout_dtype, dout_is_vector, n_valid,
+                             dlogits, B, V_local, ld, v_offset, V, ignore_index, label_smoothing,
+                             reduction, st);
+    case FO_F16:
+      return ce_bwd_t<__half>(logits, target, lse, dout, dout_dtype, dout_is_vector, n_valid,
+                              dlogits, B, V_local, ld, v_offset, V, ignore_index, label_smoothing,
+                              reduction, st);
+    default:
+      return ce_bwd_t<__nv_bfloat16>(logits, target, lse, dout, dout_dtype, dout_is_vector,
+                                     n_valid, dlogits, B, V_local, ld, v_offset, V, ignore_index,
+                                     label_smoothing, reduction, st);
+  }
+}

@@ -1,0 +1,197 @@
+"""fused_cross_entropy — drop-in for operators/fused_cross_entropy.py of Flag-Operators.
+
+Public API as the reference (fused_cross_entropy.py:302-380): fused_cross_entropy,
+cross_entropy_loss, and the autograd Function _FusedCrossEntropy.  Results follow
+torch's F.cross_entropy (the reference's CPU branch): the loss has the logits'
+dtype, 'mean' divides by the number of non-ignored rows (NaN if there are none)
+and label smoothing is computed inside the kernel.
+
+When the logits require grad, the forward kernel also writes d loss / d logits
+for grad_output == 1 while the row is still in L2; backward then only rescales
+it in place when grad_output != 1 (a kernel that exits immediately when it is
+1).  Forward + backward therefore read the logits from HBM once and write the
+gradient once.  The mean divisor is counted on the device: no host sync.
+
+Extension (keyword-only, default keeps the reference behaviour):
+``process_group=`` computes the loss of vocabulary-sharded logits: each rank
+holds columns [rank*V_local, (rank+1)*V_local) of the [B, V] logits; per-row
+(max, sum-exp, target logit, row sum) are all-gathered over NCCL and combined.
+"""
+from __future__ import annotations
+
+import logging
+
+import torch
+
+from . import _lib
+
+logger = logging.getLogger(__name__)
+
+_RED = {"none": 0, "mean": 1, "sum": 2}
+
+
+def _check(logits, target, reduction):
+    assert logits.ndim == 2, f"logits must be 2-D [B,V], got shape {logits.shape}"
+    assert reduction in ("none", "mean", "sum"), f"Unknown reduction: {reduction}"
+    B = logits.shape[0]
+    assert target.shape == (B,), f"target shape {target.shape}, expected ({B},)"
+
+
+class _FusedCrossEntropy(torch.autograd.Function):
+    """Autograd Function of the reference (fused_cross_entropy.py:241-295)."""
+
+    @staticmethod
+    def forward(ctx, logits, target, reduction, ignore_index, label_smoothing):
+        B, V = logits.shape
+        assert target.shape == (B,), f"target shape {target.shape}, expected ({B},)"
+        dev = logits.device
+        target = target.to(torch.int64).contiguous()
+        if logits.stride(1) != 1:
+            logits = logits.contiguous()
+        ld = logits.stride(0) if B > 1 else V
+        loss_rows = torch.empty(B, dtype=torch.float32, device=dev)
+        lse = torch.empty(B, dtype=torch.float32, device=dev)
+        scalar = torch.empty((), dtype=torch.float32, device=dev)
+        n_valid = torch.empty(1, dtype=torch.float32, device=dev)
+        want_grad = bool(ctx.needs_input_grad[0])
+        dlogits = torch.empty((B, V), dtype=logits.dtype, device=dev) if want_grad else None
+        _lib.call("fo_ce_fwd", _lib.ptr(logits), _lib.ptr(target), _lib.ptr(loss_rows),
+                  _lib.ptr(lse), _lib.ptr(scalar), _lib.ptr(n_valid), _lib.ptr(dlogits),
+                  B, V, ld, int(ignore_index), float(label_smoothing), _RED[reduction],
+                  _lib.dtype_code(logits.dtype), None, 0, _lib.stream_of(logits))
+        out = loss_rows if reduction == "none" else scalar
+        ctx.reduction = reduction
+        ctx.ignore_index = int(ignore_index)
+        ctx.label_smoothing = float(label_smoothing)
+        ctx.B, ctx.V, ctx.ld = B, V, ld
+        ctx.grad_ready = dlogits is not None
+        if dlogits is not None:
+            ctx.save_for_backward(logits, target, lse, n_valid, dlogits)
+        else:
+            ctx.save_for_backward(logits, target, lse, n_valid)
+        return out.to(logits.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        saved = ctx.saved_tensors
+        logits, target, lse, n_valid = saved[:4]
+        B, V = ctx.B, ctx.V
+        go = grad_output.contiguous()
+        is_vec = 1 if (ctx.reduction == "none" and go.ndim == 1) else 0
+        if ctx.grad_ready:
+            # gradient for grad_output == 1 was written by the forward pass
+            dlogits = saved[4]
+            ctx.grad_ready = False
+            _lib.call("fo_ce_scale_grad", _lib.ptr(dlogits), _lib.ptr(go),
+                      _lib.dtype_code(go.dtype), is_vec, B, V, V,
+                      _lib.dtype_code(dlogits.dtype), _lib.stream_of(dlogits))
+            return dlogits, None, None, None, None
+        dlogits = torch.empty((B, V), dtype=logits.dtype, device=logits.device)
+        _lib.call("fo_ce_bwd", _lib.ptr(logits), _lib.ptr(target), _lib.ptr(lse), _lib.ptr(go),
+                  _lib.dtype_code(go.dtype), is_vec, _lib.ptr(n_valid), _lib.ptr(dlogits),
+                  B, V, ctx.ld, ctx.ignore_index, ctx.label_smoothing, _RED[ctx.reduction],
+                  _lib.dtype_code(logits.dtype), _lib.stream_of(logits))
+        return dlogits, None, None, None, None
+
+
+class _ShardedCrossEntropy(torch.autograd.Function):
+    """Cross-entropy over vocabulary-sharded logits (one NCCL all-gather of row stats)."""
+
+    @staticmethod
+    def forward(ctx, logits, target, reduction, ignore_index, label_smoothing, group, v_offset,
+                V):
+        import torch.distributed as dist
+        B, Vn = logits.shape
+        dev = logits.device
+        logits = logits if logits.stride(1) == 1 else logits.contiguous()
+        ld = logits.stride(0) if B > 1 else Vn
+        target = target.to(torch.int64).contiguous()
+        P = dist.get_world_size(group)
+        stats = torch.empty(B, 4, dtype=torch.float32, device=dev)
+        _lib.call("fo_ce_shard_stats", _lib.ptr(logits), _lib.ptr(target), _lib.ptr(stats), B,
+                  Vn, ld, v_offset, int(ignore_index), _lib.dtype_code(logits.dtype),
+                  _lib.stream_of(logits))
+        all_stats = torch.empty(P, B, 4, dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(all_stats, stats, group=group)
+        loss_rows = torch.empty(B, dtype=torch.float32, device=dev)
+        lse = torch.empty(B, dtype=torch.float32, device=dev)
+        scalar = torch.empty((), dtype=torch.float32, device=dev)
+        n_valid = torch.empty(1, dtype=torch.float32, device=dev)
+        _lib.call("fo_ce_shard_combine", _lib.ptr(all_stats), P, _lib.ptr(target),
+                  _lib.ptr(loss_rows), _lib.ptr(lse), _lib.ptr(scalar), _lib.ptr(n_valid), B, V,
+                  int(ignore_index), float(label_smoothing), _RED[reduction],
+                  _lib.stream_of(logits))
+        ctx.save_for_backward(logits, target, lse, n_valid)
+        ctx.args = (reduction, int(ignore_index), float(label_smoothing), v_offset, V, ld)
+        out = loss_rows if reduction == "none" else scalar
+        return out.to(logits.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        logits, target, lse, n_valid = ctx.saved_tensors
+        reduction, ignore_index, ls, v_offset, V, ld = ctx.args
+        B, Vn = logits.shape
+        go = grad_output.contiguous()
+        is_vec = 1 if (reduction == "none" and go.ndim == 1) else 0
+        dlogits = torch.empty((B, Vn), dtype=logits.dtype, device=logits.device)
+        _lib.call("fo_ce_shard_bwd", _lib.ptr(logits), _lib.ptr(target), _lib.ptr(lse),
+                  _lib.ptr(go), _lib.dtype_code(go.dtype), is_vec, _lib.ptr(n_valid),
+                  _lib.ptr(dlogits), B, Vn, ld, v_offset, V, ignore_index, ls, _RED[reduction],
+                  _lib.dtype_code(logits.dtype), _lib.stream_of(logits))
+        return dlogits, None, None, None, None, None, None, None
+
+
+def fused_cross_entropy(
+    logits: torch.Tensor,
+    target: torch.Tensor,
+    reduction: str = "mean",
+    ignore_index: int = -100,
+    label_smoothing: float = 0.0,
+    *,
+    process_group=None,
+    vocab_offset: int | None = None,
+    vocab_size: int | None = None,
+) -> torch.Tensor:
+    """Fused cross-entropy (fused_cross_entropy.py:302-357).
+
+    logits [B, V], target [B] int64; reduction 'none' | 'mean' | 'sum'.
+    With process_group, logits is this rank's [B, V_local] column block; the
+    block starts at vocab_offset (default rank * V_local) of a vocabulary of
+    vocab_size columns (default V_local * world_size).
+    """
+    logger.debug("FLAG-OPS FUSED_CROSS_ENTROPY")
+    _check(logits, target, reduction)
+    _lib.require_cuda(logits, "fused_cross_entropy")
+    if not 0.0 <= float(label_smoothing) <= 1.0:
+        raise ValueError(f"label_smoothing must be in [0, 1], got {label_smoothing}")
+    if process_group is not None:
+        import torch.distributed as dist
+        rank = dist.get_rank(process_group)
+        P = dist.get_world_size(process_group)
+        Vn = logits.shape[1]
+        off = rank * Vn if vocab_offset is None else int(vocab_offset)
+        V = Vn * P if vocab_size is None else int(vocab_size)
+        return _ShardedCrossEntropy.apply(logits, target, reduction, ignore_index,
+                                          label_smoothing, process_group, off, V)
+    return _FusedCrossEntropy.apply(logits, target, reduction, ignore_index, label_smoothing)
+
+
+def cross_entropy_loss(
+    logits: torch.Tensor,
+    target: torch.Tensor,
+    weight=None,
+    reduction: str = "mean",
+    ignore_index: int = -100,
+    label_smoothing: float = 0.0,
+) -> torch.Tensor:
+    """Drop-in for F.cross_entropy (fused_cross_entropy.py:360-380).
+
+    As in the reference, a class `weight` is not fused: that case is handed to
+    torch's own cross_entropy.
+    """
+    if weight is not None:
+        return torch.nn.functional.cross_entropy(
+            logits, target, weight=weight, reduction=reduction,
+            ignore_index=ignore_index, label_smoothing=label_smoothing)
+    return fused_cross_entropy(logits, target, reduction=reduction,
+                               ignore_index=ignore_index, label_smoothing=label_smoothing)

@@ -1,0 +1,235 @@
+/*
+ * flagops.h — C ABI of the B200 (sm_100a) five-operator kernel set.
+ *
+ * Every entry point takes raw device pointers, int64 sizes, dtype codes and a
+ * cudaStream_t passed as void*.  Nothing here allocates device memory: scratch
+ * ("workspace") is owned by the caller, sized by the matching *_workspace_bytes
+ * query.  Calls are stream-ordered and never synchronise the host.  The return
+ * value is a status code (FO_OK == 0); fo_last_error() gives the message of the
+ * most recent failure on the calling thread.
+ *
+ * Each declaration names the reference (iamsuperfly/Flag-Operators) interface
+ * it replaces as path:line inside that project.
+ */
+#ifndef FLAGOPS_H
+#define FLAGOPS_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FO_API __attribute__((visibility("default")))
+#else
+#define FO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes shared by every entry point */
+enum fo_dtype {
+  FO_F32 = 0,
+  FO_F16 = 1,
+  FO_BF16 = 2,
+  FO_F64 = 3,
+  FO_I32 = 4,
+  FO_I64 = 5
+};
+
+/* status codes */
+enum fo_status {
+  FO_OK = 0,
+  FO_EINVAL = -1,       /* bad argument (shape, pointer, alignment)       */
+  FO_EDTYPE = -2,       /* dtype not supported by this entry point         */
+  FO_ECUDA = -3,        /* CUDA launch / runtime error                     */
+  FO_EWORKSPACE = -4,   /* workspace missing or too small                  */
+  FO_EUNSUPPORTED = -5  /* configuration not supported (e.g. head dim)     */
+};
+
+/* scatter_reduce reduce codes (operators/scatter_reduce.py:306) */
+enum fo_reduce {
+  FO_SUM = 0,
+  FO_PROD = 1,
+  FO_MEAN = 2,
+  FO_AMAX = 3,
+  FO_AMIN = 4
+};
+
+/* cross-entropy reduction codes (operators/fused_cross_entropy.py:325) */
+enum fo_reduction {
+  FO_RED_NONE = 0,
+  FO_RED_MEAN = 1,
+  FO_RED_SUM = 2
+};
+
+/* Message of the last failed call on this thread ("" if none). */
+FO_API const char* fo_last_error(void);
+/* ABI revision; bumped on any signature change. */
+FO_API int fo_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* rms_norm                                                                  */
+/* ------------------------------------------------------------------------ */
+/*
+ * y[m, :] = x[m, :] * inv_rms[m] * weight,  inv_rms[m] = 1/sqrt(mean(x[m,:]^2) + eps)
+ * x, y: [M, N] contiguous (x_dtype); weight: [N] (w_dtype); inv_rms: [M] fp32.
+ * Replaces rms_norm_forward, operators/rms_norm.py:186-228 (and its kernels
+ * _rms_norm_small_kernel rms_norm.py:50-90, _rms_norm_loop_kernel rms_norm.py:97-176).
+ */
+FO_API int fo_rms_norm_fwd(const void* x, const void* weight, void* y, float* inv_rms,
+                    int64_t M, int64_t N, float eps, int x_dtype, int w_dtype,
+                    void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* median                                                                    */
+/* ------------------------------------------------------------------------ */
+/*
+ * Lower median of each row of x [M, N] (contiguous): values [M] (dtype of x),
+ * indices [M] int64, with torch CPU semantics: the index is the k-th entry
+ * (k = (N-1)/2) of a stable ascending sort, -0.0 == +0.0, and any NaN in a
+ * row gives NaN with the index of the row's first NaN.
+ * Replaces _median_dim, operators/median.py:241-305 (kernels median.py:82-192).
+ */
+FO_API int fo_median_dim(const void* x, void* values, int64_t* indices, int64_t M,
+                  int64_t N, int dtype, void* stream);
+
+/*
+ * Lower median of all n elements of x (contiguous), written to value[0]
+ * (dtype of x).  Replaces _median_global, operators/median.py:308-325.
+ * workspace: fo_median_all_workspace_bytes(n) bytes.
+ */
+FO_API int fo_median_all_workspace_bytes(int64_t n, int64_t* bytes);
+FO_API int fo_median_all(const void* x, void* value, int64_t n, int dtype,
+                  void* workspace, int64_t ws_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* scatter_reduce                                                            */
+/* ------------------------------------------------------------------------ */
+/*
+ * out[..., index[p], ...] = reduce(out[...], src[p]) along `dim` for every
+ * position p of index (torch.Tensor.scatter_reduce_ semantics).  `out` holds
+ * self's values on entry (the caller copies self into it for the out-of-place
+ * and out= variants).  ndim in [1, 4]; index_shape / index_strides /
+ * src_strides / out_shape / out_strides are ndim-long arrays, strides in
+ * elements.  Indices outside [0, out_shape[dim]) are skipped and counted into
+ * *err_count (device int32, nullable).
+ * Replaces scatter_reduce_ / scatter_reduce / scatter_reduce_out and their
+ * launcher, operators/scatter_reduce.py:327-468 (kernels 69-276).
+ */
+FO_API int fo_scatter_reduce_workspace_bytes(int64_t out_numel, int reduce,
+                                      int include_self, int dtype,
+                                      int64_t* bytes);
+FO_API int fo_scatter_reduce(void* out, const void* src, const void* index, int ndim,
+                      const int64_t* index_shape, const int64_t* index_strides,
+                      const int64_t* src_strides, const int64_t* out_shape,
+                      const int64_t* out_strides, int dim, int reduce,
+                      int include_self, int dtype, int index_dtype,
+                      void* workspace, int64_t ws_bytes, int32_t* err_count,
+                      void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* fused cross-entropy                                                       */
+/* ------------------------------------------------------------------------ */
+/*
+ * Forward over logits [B, V] (row stride ld elements, dtype) and target [B]
+ * int64.  Writes per-row loss loss_rows [B] fp32 (0 for ignored rows), lse [B]
+ * fp32, and out_scalar[0] fp32 = sum (FO_RED_SUM) or sum / n_valid
+ * (FO_RED_MEAN; NaN when every row is ignored, as torch); n_valid_out[0] fp32 =
+ * number of rows whose target != ignore_index.  label_smoothing in [0, 1) is
+ * fused (loss = lse - (1-e) x_t - e mean(x)).  When dlogits (contiguous
+ * [B, V], logits' dtype) is non-null the
+ * gradient d loss / d logits for grad_output == 1 is written in the same pass
+ * (row re-read from L2), so a later fo_ce_scale_grad completes backward.
+ * workspace: fo_ce_workspace_bytes(B) bytes.
+ * Replaces _FusedCrossEntropy.forward, operators/fused_cross_entropy.py:243-274,
+ * and _fused_ce_fwd_kernel (fused_cross_entropy.py:63-148).
+ */
+FO_API int fo_ce_workspace_bytes(int64_t B, int64_t* bytes);
+FO_API int fo_ce_fwd(const void* logits, const int64_t* target, float* loss_rows,
+              float* lse, float* out_scalar, float* n_valid_out, void* dlogits,
+              int64_t B, int64_t V, int64_t ld, int64_t ignore_index,
+              float label_smoothing, int reduction, int dtype, void* workspace,
+              int64_t ws_bytes, void* stream);
+
+/*
+ * Backward by recomputation: dlogits = dout * (softmax(x) - (1-e) onehot - e/V)
+ * / (n_valid for mean), 0 on ignored rows; dlogits is contiguous [B, V].
+ * dout is a device scalar
+ * (dout_is_vector == 0) or a [B] vector (reduction none).
+ * Replaces _FusedCrossEntropy.backward, fused_cross_entropy.py:276-295, and
+ * _fused_ce_bwd_kernel (fused_cross_entropy.py:155-234).
+ */
+FO_API int fo_ce_bwd(const void* logits, const int64_t* target, const float* lse,
+              const void* dout, int dout_dtype, int dout_is_vector,
+              const float* n_valid, void* dlogits, int64_t B, int64_t V,
+              int64_t ld, int64_t ignore_index, float label_smoothing,
+              int reduction, int dtype, void* stream);
+
+/*
+ * dlogits *= dout (device scalar, dout_dtype) or dlogits[b, :] *= dout[b]
+ * (dout_is_vector); a no-op pass-through when the scalar is exactly 1.
+ * Completes backward after fo_ce_fwd wrote the gradient.
+ */
+FO_API int fo_ce_scale_grad(void* dlogits, const void* dout, int dout_dtype,
+                     int dout_is_vector, int64_t B, int64_t V, int64_t ld,
+                     int dtype, void* stream);
+
+/*
+ * Vocabulary-sharded forward, step 1 (no reference counterpart; the reference
+ * is single-device): per-row statistics of this rank's column slice
+ * [B, V_local] whose first column is global column v_offset.
+ * stats [B, 4] fp32 = (row max, sum exp(x - max), target logit or 0,
+ * row sum of logits).
+ */
+FO_API int fo_ce_shard_stats(const void* logits, const int64_t* target, float* stats,
+                      int64_t B, int64_t V_local, int64_t ld, int64_t v_offset,
+                      int64_t ignore_index, int dtype, void* stream);
+/*
+ * Step 2, after the stats of all P ranks were gathered into
+ * all_stats [P, B, 4]: combine into lse [B], loss_rows [B], out_scalar,
+ * n_valid_out, exactly as fo_ce_fwd does for one rank.  V is the full vocab.
+ */
+FO_API int fo_ce_shard_combine(const float* all_stats, int P, const int64_t* target,
+                        float* loss_rows, float* lse, float* out_scalar,
+                        float* n_valid_out, int64_t B, int64_t V,
+                        int64_t ignore_index, float label_smoothing,
+                        int reduction, void* stream);
+/*
+ * Step 3: this rank's slice of the gradient (as fo_ce_bwd, columns offset by
+ * v_offset, softmax normalised by the global lse).
+ */
+FO_API int fo_ce_shard_bwd(const void* logits, const int64_t* target, const float* lse,
+                    const void* dout, int dout_dtype, int dout_is_vector,
+                    const float* n_valid, void* dlogits, int64_t B,
+                    int64_t V_local, int64_t ld, int64_t v_offset, int64_t V,
+                    int64_t ignore_index, float label_smoothing, int reduction,
+                    int dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* chunk_gated_delta_rule                                                    */
+/* ------------------------------------------------------------------------ */
+/*
+ * h_t = g_t h_{t-1} + beta_t (v_t - h_{t-1} k_t) k_t^T,  o_t = h_t q_t
+ * q, k, v, o: [B, H, L, D] contiguous (dtype); beta, g: [B, H, L] (gate_dtype);
+ * h0: [B, H, D, D] fp32 initial state or NULL (zeros); hT: [B, H, D, D] fp32
+ * final state or NULL.  D in {16, 32, 64, 128}.  D = 128 with bf16/fp16 runs
+ * the chunked tcgen05 kernel; the other cases run the per-step kernel.
+ * Replaces chunk_gated_delta_rule, operators/chunk_gated_delta_rule.py:208-268
+ * (kernels chunk_gated_delta_rule.py:71-191).
+ */
+FO_API int fo_gdr_fwd(const void* q, const void* k, const void* v, const void* beta,
+               const void* g, const float* h0, void* o, float* hT, int64_t B,
+               int64_t H, int64_t L, int64_t D, int dtype, int gate_dtype,
+               void* stream);
+/* Same recurrence, always through the per-step CUDA-core kernel (any D in
+ * {16,32,64,128}); kept as an independent on-device cross-check. */
+FO_API int fo_gdr_fwd_stepwise(const void* q, const void* k, const void* v,
+                        const void* beta, const void* g, const float* h0,
+                        void* o, float* hT, int64_t B, int64_t H, int64_t L,
+                        int64_t D, int dtype, int gate_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLAGOPS_H */

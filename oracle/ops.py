@@ -1,0 +1,162 @@
+"""CPU restatement of the reference's CPU path (test infrastructure only).
+
+Each function names the reference lines it restates (paths inside the
+iamsuperfly/Flag-Operators project).  The reference's CPU branch is plain torch
+on CPU tensors; the restatement keeps exactly that arithmetic so its outputs are
+the reference's outputs.  `median_dim_np` is an independent numpy statement of
+torch's median index rule, used to pin the semantics the kernels must match.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+
+def _cpu(t):
+    return t.detach().cpu() if isinstance(t, torch.Tensor) else t
+
+
+# ---------------------------------------------------------------------------
+# rms_norm — operators/rms_norm.py:201-216 (CPU fallback branch)
+# ---------------------------------------------------------------------------
+def rms_norm_forward(x, normalized_shape, weight, eps=1e-5):
+    """(y, inv_rms) exactly as rms_norm.py:209-216 computes them on CPU."""
+    x = _cpu(x)
+    weight = _cpu(weight)
+    if isinstance(normalized_shape, int):
+        normalized_shape = (normalized_shape,)
+    N = math.prod(normalized_shape)          # rms_norm.py:201
+    M = x.numel() // N                       # rms_norm.py:202
+    x = x.contiguous()                       # rms_norm.py:204
+    weight = weight.contiguous().view(-1)    # rms_norm.py:205
+    y = torch.empty_like(x)                  # rms_norm.py:206
+    inv_rms = torch.empty(M, dtype=torch.float32)
+    xf = x.float().view(M, N)                                    # rms_norm.py:211
+    rms = torch.sqrt((xf * xf).mean(dim=-1, keepdim=True) + eps)  # rms_norm.py:212
+    yf = (xf / rms) * weight.float()                             # rms_norm.py:213
+    y.copy_(yf.view_as(x))                                       # rms_norm.py:214
+    inv_rms.copy_(1.0 / rms.squeeze(-1))                         # rms_norm.py:215
+    return y, inv_rms
+
+
+# ---------------------------------------------------------------------------
+# median — operators/median.py:348-352 (CPU branch: torch.median)
+# ---------------------------------------------------------------------------
+def median(inp, dim=None, keepdim=False):
+    inp = _cpu(inp)
+    if dim is None:
+        return torch.median(inp)                                  # median.py:350-351
+    return torch.median(inp, dim=dim, keepdim=keepdim)            # median.py:352
+
+
+def median_dim_np(x2d: np.ndarray):
+    """Independent statement of torch CPU's median-along-dim rule for a 2-D array.
+
+    values, indices of each row: k = (N-1)//2; the index is the k-th entry of a
+    stable ascending sort (ties keep index order, -0.0 == +0.0); a row holding a
+    NaN yields NaN and the index of its first NaN.
+    """
+    x2d = np.asarray(x2d)
+    M, N = x2d.shape
+    k = (N - 1) // 2
+    order = np.argsort(x2d, axis=1, kind="stable")
+    idx = order[:, k].astype(np.int64)
+    isnan = np.isnan(x2d) if np.issubdtype(x2d.dtype, np.floating) else np.zeros_like(x2d, bool)
+    has_nan = isnan.any(axis=1)
+    if has_nan.any():
+        first_nan = np.argmax(isnan, axis=1)
+        idx = np.where(has_nan, first_nan, idx)
+    vals = x2d[np.arange(M), idx]
+    return vals, idx
+
+
+# ---------------------------------------------------------------------------
+# scatter_reduce — operators/scatter_reduce.py:397-398, 427-429, 457-459
+# ---------------------------------------------------------------------------
+def scatter_reduce_(inp, dim, index, src, reduce, *, include_self=True):
+    return _cpu(inp).clone().scatter_reduce_(dim, _cpu(index), _cpu(src), reduce,
+                                             include_self=include_self)
+
+
+def scatter_reduce(inp, dim, index, src, reduce, *, include_self=True):
+    return torch.scatter_reduce(_cpu(inp), dim, _cpu(index), _cpu(src), reduce,
+                                include_self=include_self)
+
+
+def scatter_reduce_out(out, inp, dim, index, src, reduce, *, include_self=True):
+    out_c = torch.empty_like(_cpu(out))
+    return torch.scatter_reduce(_cpu(inp), dim, _cpu(index), _cpu(src), reduce,
+                                include_self=include_self, out=out_c)
+
+
+def scatter_reduce_scale(inp, dim, index, src, include_self=True):
+    """Per-cell (sum of |terms|, number of terms) in float64, for tolerances.
+
+    A float sum's rounding error is bounded by a multiple of the sum of the
+    magnitudes of its terms, so parity of float sum/mean is checked against
+    rtol * this scale rather than rtol * |result|.
+    """
+    inp = _cpu(inp).double()
+    index = _cpu(index)
+    src = _cpu(src).double()
+    base_abs = inp.abs() if include_self else torch.zeros_like(inp)
+    base_cnt = torch.ones_like(inp) if include_self else torch.zeros_like(inp)
+    scale = base_abs.scatter_add(dim, index, src.abs()[tuple(slice(0, s) for s in index.shape)])
+    cnt = base_cnt.scatter_add(dim, index, torch.ones(index.shape, dtype=torch.float64))
+    return scale, cnt
+
+
+# ---------------------------------------------------------------------------
+# fused_cross_entropy — operators/fused_cross_entropy.py:327-331 (F.cross_entropy)
+# ---------------------------------------------------------------------------
+def fused_cross_entropy(logits, target, reduction="mean", ignore_index=-100, label_smoothing=0.0):
+    return F.cross_entropy(_cpu(logits), _cpu(target), reduction=reduction,
+                           ignore_index=ignore_index, label_smoothing=label_smoothing)
+
+
+def fused_cross_entropy_grad(logits, target, reduction="mean", ignore_index=-100,
+                             label_smoothing=0.0, grad_output=None):
+    """(loss, dlogits) of the CPU branch via autograd (fused_cross_entropy.py:327-331)."""
+    lg = _cpu(logits).clone().requires_grad_(True)
+    loss = F.cross_entropy(lg, _cpu(target), reduction=reduction, ignore_index=ignore_index,
+                           label_smoothing=label_smoothing)
+    go = torch.ones_like(loss) if grad_output is None else _cpu(grad_output).to(loss.dtype)
+    loss.backward(go)
+    return loss.detach(), lg.grad.detach()
+
+
+# ---------------------------------------------------------------------------
+# chunk_gated_delta_rule — _ref_forward, operators/chunk_gated_delta_rule.py:275-310
+# ---------------------------------------------------------------------------
+def delta_rule_forward(q, k, v, beta, g, initial_state=None, output_final_state=False):
+    """Sequential fp32 recurrence of _ref_forward (chunk_gated_delta_rule.py:286-310).
+
+    h_t = g_t h_{t-1} + beta_t (v_t - h_{t-1} k_t) k_t^T ;  o_t = h_t q_t (cast to q's dtype).
+    Extends the reference with an optional fp32 initial state [B,H,D,D] and
+    returns (o, h_T) when output_final_state is set.
+    """
+    q, k, v, beta, g = (_cpu(t) for t in (q, k, v, beta, g))
+    B, H, L, D = q.shape
+    dtype = q.dtype
+    if initial_state is None:
+        h = torch.zeros(B, H, D, D, dtype=torch.float32)                 # :288
+    else:
+        h = _cpu(initial_state).float().clone()
+    o = torch.empty_like(q)                                               # :289
+    for t in range(L):                                                    # :291
+        q_t = q[:, :, t, :].float()                                       # :292
+        k_t = k[:, :, t, :].float()                                       # :293
+        v_t = v[:, :, t, :].float()                                       # :294
+        beta_t = beta[:, :, t]                                            # :295
+        g_t = g[:, :, t]                                                  # :296
+        residual = (h @ k_t.unsqueeze(-1)).squeeze(-1)                    # :299
+        delta = v_t - residual                                            # :300
+        h = (g_t[:, :, None, None] * h                                    # :303-305
+             + beta_t[:, :, None, None] * (delta.unsqueeze(-1) * k_t.unsqueeze(-2)))
+        o[:, :, t, :] = (h @ q_t.unsqueeze(-1)).squeeze(-1).to(dtype)     # :308
+    if output_final_state:
+        return o, h
+    return o

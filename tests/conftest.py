@@ -1,0 +1,48 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(REPO, "flag-operators_b200")
+for p in (PKG, REPO):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+GOLDEN = os.path.join(REPO, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def pytest_collection_modifyitems(config, items):
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for it in items:
+        if "gpu" in it.keywords:
+            it.add_marker(skip)
+
+
+def load_golden(name: str) -> dict:
+    """Loads tests/golden/<name>.npz as torch tensors (bf16 keys decoded)."""
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    out = {}
+    for k in z.files:
+        a = z[k]
+        if k.endswith("__bf16"):
+            out[k[:-6]] = torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
+        elif a.ndim == 0 and a.dtype.kind in "fiub":
+            out[k] = a.item()
+            out[k + "__t"] = torch.from_numpy(np.array(a))
+        else:
+            out[k] = torch.from_numpy(a.copy())
+    return out
+
+
+@pytest.fixture(scope="session")
+def golden():
+    return load_golden

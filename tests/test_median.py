@@ -1,0 +1,133 @@
+"""median parity: values AND indices bit-exact against the oracle (torch CPU
+median, the reference's CPU branch), on the golden fixtures, the three full-size
+configurations and the edge cases torch defines (ties, -0/+0, NaN, inf)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import load_golden
+from operators.median import median
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _exact(x_cpu, dim=-1, keepdim=False):
+    got = median(x_cpu.to(DEV), dim=dim, keepdim=keepdim)
+    ref = oracle.median(x_cpu, dim=dim, keepdim=keepdim)
+    assert got.values.shape == ref.values.shape and got.indices.shape == ref.indices.shape
+    assert torch.equal(got.indices.cpu(), ref.indices), "indices differ"
+    gv, rv = got.values.cpu(), ref.values
+    if gv.dtype.is_floating_point:
+        same = (gv.view(-1).float().isnan() & rv.view(-1).float().isnan()) | (
+            gv.view(-1) == rv.view(-1))
+        assert bool(same.all()), "values differ"
+        # bit-exact where not NaN (x[idx] itself)
+        nn = ~rv.view(-1).float().isnan()
+        assert torch.equal(gv.view(-1)[nn].view(torch.int16 if gv.element_size() == 2
+                                                else torch.int32),
+                           rv.view(-1)[nn].view(torch.int16 if rv.element_size() == 2
+                                                else torch.int32))
+    else:
+        assert torch.equal(gv, rv)
+
+
+def test_golden_fixtures():
+    z = load_golden("median")
+    for name in ("a", "b", "c", "s"):
+        got = median(z[f"x_{name}"].to(DEV), dim=-1)
+        assert torch.equal(got.indices.cpu(), z[f"i_{name}"]), name
+        assert np.array_equal(got.values.cpu().numpy(), z[f"v_{name}"].numpy(), equal_nan=True)
+    for d in (0, 1, 2):
+        got = median(z["x3"].to(DEV), dim=d)
+        assert torch.equal(got.values.cpu(), z[f"v3_{d}"])
+        assert torch.equal(got.indices.cpu(), z[f"i3_{d}"])
+    for i in range(z["n_known"]):
+        assert torch.equal(median(z[f"kx{i}"].to(DEV)).cpu(), z[f"kv{i}"])
+    assert torch.equal(median(z["gx"].to(DEV)).cpu(), z["gv"])
+
+
+@pytest.mark.parametrize("cfg", ["a", "b", "c"])
+def test_baseline_configs(cfg):
+    g = torch.Generator().manual_seed(0)
+    if cfg == "a":
+        x = torch.randn(8192, 2048, generator=g)
+    elif cfg == "b":
+        x = torch.randint(-64, 64, (8192, 2048), generator=g).float()
+    else:
+        x = torch.randn(65536, 257, generator=g)
+    _exact(x)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.int32, torch.int64,
+                                   torch.int16, torch.uint8])
+@pytest.mark.parametrize("N", [1, 2, 31, 257, 1024, 2048, 5000])
+def test_dtypes(dtype, N):
+    if dtype.is_floating_point:
+        x = torch.randn(64, N).to(dtype)
+    else:
+        lo = 0 if dtype == torch.uint8 else -50
+        x = torch.randint(lo, 50, (64, N)).to(dtype)
+    _exact(x)
+
+
+@pytest.mark.parametrize("N", [1, 2, 3, 32, 33, 127, 128, 129, 511, 512, 513, 2047, 2048, 2049,
+                               4096, 10000, 70000])
+def test_lengths_fp32(N):
+    _exact(torch.randn(37, N))
+    _exact(torch.randint(-3, 3, (37, N)).float())   # very tie-heavy
+
+
+def test_special_values():
+    x = torch.randn(64, 300)
+    x[0] = 0.0
+    x[1, ::2] = -0.0
+    x[2, 5] = float("nan")
+    x[3, 100:] = float("nan")
+    x[4] = float("inf")
+    x[5, :150] = float("-inf")
+    x[6, 7] = float("nan"); x[6, 3] = float("nan")
+    x[7] = torch.where(torch.rand(300) < 0.5, torch.tensor(-0.0), torch.tensor(0.0))
+    _exact(x)
+    xv = x.clone()[:, :256].contiguous()    # vector (16-byte) load path
+    _exact(xv)
+
+
+def test_dims_and_keepdim():
+    x = torch.randn(4, 8, 16, 5)
+    for d in range(-4, 4):
+        for kd in (False, True):
+            _exact(x, dim=d, keepdim=kd)
+    _exact(torch.randn(7), dim=0)
+    got = median(torch.tensor([5.0, 3.0, 1.0, 4.0, 2.0], device=DEV), dim=0)
+    assert got.values.item() == 3.0 and got.indices.item() == 1
+
+
+def test_global_median():
+    for shape in [(1,), (7,), (16,), (4, 128, 128), (1000003,)]:
+        x = torch.randn(*shape)
+        assert torch.equal(median(x.to(DEV)).cpu(), oracle.median(x))
+    xh = torch.randn(64).half()
+    assert torch.equal(median(xh.to(DEV)).cpu(), oracle.median(xh))
+    xn = torch.randn(100)
+    xn[17] = float("nan")
+    assert torch.isnan(median(xn.to(DEV))).item()
+    with pytest.raises(RuntimeError, match="must not be empty"):
+        median(torch.empty(0, device=DEV))
+
+
+def test_non_contiguous_input():
+    x = torch.randn(300, 64).t()     # [64, 300] view with stride (1, 64)
+    _exact(x)
+
+
+def test_empty_rows():
+    got = median(torch.empty(0, 5, device=DEV), dim=1)
+    assert got.values.shape == (0,) and got.indices.shape == (0,)
+
+
+def test_deterministic():
+    x = torch.randint(-5, 5, (512, 999)).float().to(DEV)
+    a, b = median(x, dim=1), median(x, dim=1)
+    assert torch.equal(a.indices, b.indices)
