@@ -438,7 +438,7 @@ extern "C" int fo_ce_fwd(const void* logits, const int64_t* target, float* loss_
   if (int rc = check_common(logits, target, B, V, ld, dtype, "fo_ce_fwd")) return rc;
   FO_CHECK_ARG(reduction >= FO_RED_NONE && reduction <= FO_RED_SUM, "fo_ce_fwd: bad reduction %d",
                reduction);
-  FO_CHECK_ARG(loss_rows && lse && n_valid_out, "fo_ce_fwd: null output pointer");
+  FO_CHECK_ARG(n_valid_out && (B == 0 || (loss_rows && lse)), "fo_ce_fwd: null output pointer");
   FO_CHECK_ARG(reduction == FO_RED_NONE || out_scalar, "fo_ce_fwd: null out_scalar");
   FO_CHECK_ARG(label_smoothing >= 0.f && label_smoothing <= 1.f, "fo_ce_fwd: bad label_smoothing");
   cudaStream_t st = as_stream(stream);

@@ -1,0 +1,533 @@
+// scatter_reduce (sum, prod, mean, amax, amin; include_self) for sm_100a.
+//
+// Semantics: torch.Tensor.scatter_reduce_ on CPU (the reference's CPU branch,
+// operators/scatter_reduce.py:397-398, 427-429, 457-459):
+//   for every position p of index: out[p with p[dim] := index[p]] op= src[p]
+//   include_self=False: a cell reached by >= 1 index takes the reduction of its
+//     src values only; cells never reached keep self.
+//   mean: sum / count (count includes self when include_self); integer mean
+//     rounds toward -inf.  amax/amin propagate NaN.
+//
+// Design.
+//  * One pass over (index, src): 16-byte vector loads on the contiguous 1-D
+//    path, generic strided addressing for 2-4-D.
+//  * Each CTA keeps a shared-memory cache of output cells (hashed slots, tag =
+//    output offset).  An update whose cell owns a slot is a shared-memory
+//    atomic; others go straight to global atomics (L2).  At the end the CTA
+//    flushes its slots with one global atomic each.  Skewed (Zipf) indices —
+//    thousands of updates on a few cells — thus cost shared-memory atomics
+//    instead of serialised same-address L2 atomics; uniform indices pass
+//    through with one extra shared-memory probe.
+//  * Float amax/amin reduce order-preserving uint32 keys with native integer
+//    atomicMax/Min (no CAS loop); NaN maps to the extreme key so it wins.
+//    prod is the only CAS loop.
+//  * A scratch accumulator (+ int32 counts) is used only when needed:
+//    include_self=False (to know which cells were reached), mean (counts),
+//    float amax/amin (keys) and 16-bit floats (fp32 accumulation).  Then an
+//    init pass and a finalize pass run over the output (1/16 of the traffic of
+//    the scatter pass at the benchmark shape).
+#include <limits.h>
+
+#include "common.cuh"
+
+namespace fo {
+namespace {
+
+enum Op { kSum = FO_SUM, kProd = FO_PROD, kMean = FO_MEAN, kAmax = FO_AMAX, kAmin = FO_AMIN };
+
+constexpr int kThreads = 512;
+template <typename A> struct Slots { static constexpr int kLog = sizeof(A) == 8 ? 11 : 12; static constexpr int kN = 1 << kLog; };
+constexpr uint32_t kEmpty = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// value <-> accumulator conversions
+// ---------------------------------------------------------------------------
+template <typename T> __device__ __forceinline__ float tof(T v) { return to_f<T>(v); }
+template <> __device__ __forceinline__ float tof<int32_t>(int32_t v) { return (float)v; }
+template <> __device__ __forceinline__ float tof<int64_t>(int64_t v) { return (float)v; }
+
+__device__ __forceinline__ uint32_t fkey(float x, bool nan_high) {
+  if (x != x) return nan_high ? 0xffffffffu : 0u;
+  const uint32_t u = __float_as_uint(x);
+  return u ^ ((uint32_t)((int32_t)u >> 31) | 0x80000000u);
+}
+__device__ __forceinline__ float funkey(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k ^ 0x80000000u) : ~k;
+  return __uint_as_float(u);
+}
+
+// Accumulator traits: A is the type atomics operate on.
+template <typename T, int OP, bool KEYS> struct Acc;
+
+// float amax/amin through keys
+template <typename T, int OP> struct Acc<T, OP, true> {
+  using A = uint32_t;
+  static __device__ __forceinline__ A identity() { return OP == kAmax ? 0u : 0xffffffffu; }
+  static __device__ __forceinline__ A from(T v) { return fkey(tof<T>(v), OP == kAmax); }
+  static __device__ __forceinline__ void op(A* p, A v) {
+    if (OP == kAmax) atomicMax(p, v);
+    else atomicMin(p, v);
+  }
+};
+
+template <typename A> __device__ __forceinline__ void atomic_add_a(A* p, A v);
+template <> __device__ __forceinline__ void atomic_add_a<float>(float* p, float v) { atomicAdd(p, v); }
+template <> __device__ __forceinline__ void atomic_add_a<int32_t>(int32_t* p, int32_t v) { atomicAdd(p, v); }
+template <> __device__ __forceinline__ void atomic_add_a<int64_t>(int64_t* p, int64_t v) {
+  atomicAdd(reinterpret_cast<unsigned long long*>(p), (unsigned long long)v);
+}
+template <typename A> __device__ __forceinline__ void atomic_mul_a(A* p, A v);
+template <> __device__ __forceinline__ void atomic_mul_a<float>(float* p, float v) {
+  unsigned int* q = reinterpret_cast<unsigned int*>(p);
+  unsigned int old = *reinterpret_cast<volatile unsigned int*>(q), assumed;
+  do {
+    assumed = old;
+    old = atomicCAS(q, assumed, __float_as_uint(__uint_as_float(assumed) * v));
+  } while (old != assumed);
+}
+template <> __device__ __forceinline__ void atomic_mul_a<int32_t>(int32_t* p, int32_t v) {
+  int old = *reinterpret_cast<volatile int*>(p), assumed;
+  do {
+    assumed = old;
+    old = atomicCAS(p, assumed, (int)((uint32_t)assumed * (uint32_t)v));
+  } while (old != assumed);
+}
+template <> __device__ __forceinline__ void atomic_mul_a<int64_t>(int64_t* p, int64_t v) {
+  unsigned long long* q = reinterpret_cast<unsigned long long*>(p);
+  unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(q), assumed;
+  do {
+    assumed = old;
+    old = atomicCAS(q, assumed, (unsigned long long)((uint64_t)assumed * (uint64_t)v));
+  } while (old != assumed);
+}
+__device__ __forceinline__ void atomic_max_a(int32_t* p, int32_t v) { atomicMax(p, v); }
+__device__ __forceinline__ void atomic_min_a(int32_t* p, int32_t v) { atomicMin(p, v); }
+__device__ __forceinline__ void atomic_max_a(int64_t* p, int64_t v) {
+  atomicMax(reinterpret_cast<long long*>(p), (long long)v);
+}
+__device__ __forceinline__ void atomic_min_a(int64_t* p, int64_t v) {
+  atomicMin(reinterpret_cast<long long*>(p), (long long)v);
+}
+
+template <typename T> struct AccType { using A = T; };
+template <> struct AccType<__half> { using A = float; };
+template <> struct AccType<__nv_bfloat16> { using A = float; };
+
+template <typename T, int OP> struct Acc<T, OP, false> {
+  using A = typename AccType<T>::A;
+  static __device__ __forceinline__ A identity() {
+    if (OP == kProd) return (A)1;
+    if (OP == kAmax) return sizeof(A) == 8 ? (A)LLONG_MIN : (A)INT_MIN;
+    if (OP == kAmin) return sizeof(A) == 8 ? (A)LLONG_MAX : (A)INT_MAX;
+    return (A)0;
+  }
+  static __device__ __forceinline__ A from(T v);
+  static __device__ __forceinline__ void op(A* p, A v) {
+    if (OP == kSum || OP == kMean) atomic_add_a<A>(p, v);
+    else if (OP == kProd) atomic_mul_a<A>(p, v);
+    else if constexpr (sizeof(A) == 4 && !std::is_same<A, float>::value) {
+      if (OP == kAmax) atomic_max_a((int32_t*)p, (int32_t)v);
+      else atomic_min_a((int32_t*)p, (int32_t)v);
+    } else if constexpr (sizeof(A) == 8) {
+      if (OP == kAmax) atomic_max_a((int64_t*)p, (int64_t)v);
+      else atomic_min_a((int64_t*)p, (int64_t)v);
+    }
+  }
+};
+template <typename T, int OP>
+__device__ __forceinline__ typename Acc<T, OP, false>::A Acc<T, OP, false>::from(T v) {
+  if constexpr (std::is_same<A, float>::value) return tof<T>(v);
+  else return (A)v;
+}
+
+// ---------------------------------------------------------------------------
+// the scatter pass
+// ---------------------------------------------------------------------------
+struct Geo {
+  int64_t shape[4];    // index shape (padded with 1)
+  int64_t istr[4];     // index strides
+  int64_t sstr[4];     // src strides
+  int64_t ostr[4];     // out strides
+  int64_t out_dim;     // out.shape[dim]
+  int dim;
+  int ndim;
+};
+
+template <typename T, typename I, int OP, bool KEYS, bool CNT, int NDIM, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+scatter_kernel(const T* __restrict__ src, const I* __restrict__ index,
+               typename Acc<T, OP, KEYS>::A* __restrict__ acc, int32_t* __restrict__ cnt,
+               int64_t n, Geo g, int32_t* __restrict__ err, bool use_cache) {
+  using AT = Acc<T, OP, KEYS>;
+  using A = typename AT::A;
+  constexpr int kSlots = Slots<A>::kN;
+  __shared__ uint32_t s_tag[kSlots];
+  __shared__ A s_val[kSlots];
+  __shared__ int32_t s_cnt[CNT ? kSlots : 1];
+  if (use_cache) {
+    for (int j = threadIdx.x; j < kSlots; j += blockDim.x) {
+      s_tag[j] = kEmpty;
+      s_val[j] = AT::identity();
+      if (CNT) s_cnt[j] = 0;
+    }
+    __syncthreads();
+  }
+  int32_t bad = 0;
+
+  auto update = [&](int64_t off, A v) {
+    if (use_cache) {
+      const uint32_t o32 = (uint32_t)off;
+      const uint32_t slot = (o32 * 2654435761u) >> (32 - Slots<A>::kLog);
+      uint32_t t = s_tag[slot];
+      if (t == kEmpty) {
+        const uint32_t prev = atomicCAS(&s_tag[slot], kEmpty, o32);
+        t = (prev == kEmpty) ? o32 : prev;
+      }
+      if (t == o32) {
+        AT::op(&s_val[slot], v);
+        if (CNT) atomicAdd(&s_cnt[slot], 1);
+        return;
+      }
+    }
+    AT::op(acc + off, v);
+    if (CNT) atomicAdd(cnt + off, 1);
+  };
+
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (VEC) {
+    // 1-D, contiguous index (int64) and src, 16-byte aligned: 4 elements / thread
+    static_assert(!VEC || sizeof(I) == 8, "vector path expects int64 index");
+    const int64_t nq = n / 4;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nq; q += stride) {
+      const uint4 i01 = ld_global_stream_v4(index + q * 4);
+      const uint4 i23 = ld_global_stream_v4(index + q * 4 + 2);
+      T sv[4];
+      if (sizeof(T) == 4) {
+        const uint4 s4 = ld_global_stream_v4(src + q * 4);
+        memcpy(sv, &s4, 16);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sv[e] = src[q * 4 + e];
+      }
+      int64_t iv[4];
+      iv[0] = (int64_t)(((uint64_t)i01.y << 32) | i01.x);
+      iv[1] = (int64_t)(((uint64_t)i01.w << 32) | i01.z);
+      iv[2] = (int64_t)(((uint64_t)i23.y << 32) | i23.x);
+      iv[3] = (int64_t)(((uint64_t)i23.w << 32) | i23.z);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (iv[e] < 0 || iv[e] >= g.out_dim) { ++bad; continue; }
+        update(iv[e] * g.ostr[0], AT::from(sv[e]));
+      }
+    }
+    for (int64_t p = nq * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += stride) {
+      const int64_t iv = (int64_t)index[p];
+      if (iv < 0 || iv >= g.out_dim) { ++bad; continue; }
+      update(iv * g.ostr[0], AT::from(src[p]));
+    }
+  } else {
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += stride) {
+      int64_t c[4] = {0, 0, 0, 0};
+      int64_t rem = p;
+#pragma unroll
+      for (int d = NDIM - 1; d >= 0; --d) {
+        c[d] = rem % g.shape[d];
+        rem /= g.shape[d];
+      }
+      int64_t io = 0, so = 0, oo = 0;
+#pragma unroll
+      for (int d = 0; d < NDIM; ++d) {
+        io += c[d] * g.istr[d];
+        so += c[d] * g.sstr[d];
+        if (d != g.dim) oo += c[d] * g.ostr[d];
+      }
+      const int64_t iv = (int64_t)index[io];
+      if (iv < 0 || iv >= g.out_dim) { ++bad; continue; }
+      update(oo + iv * g.ostr[g.dim], AT::from(src[so]));
+    }
+  }
+
+  if (bad && err) atomicAdd(err, bad);
+  if (use_cache) {
+    __syncthreads();
+    for (int j = threadIdx.x; j < kSlots; j += blockDim.x) {
+      const uint32_t t = s_tag[j];
+      if (t != kEmpty) {
+        AT::op(acc + t, s_val[j]);
+        if (CNT) atomicAdd(cnt + t, s_cnt[j]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// init / finalize over the output (out may be strided: walk its logical shape)
+// ---------------------------------------------------------------------------
+struct OutGeo {
+  int64_t shape[4];
+  int64_t str[4];
+  int ndim;
+  int64_t numel;
+};
+
+__device__ __forceinline__ int64_t out_offset(const OutGeo& o, int64_t i) {
+  int64_t off = 0;
+  for (int d = o.ndim - 1; d >= 0; --d) {
+    off += (i % o.shape[d]) * o.str[d];
+    i /= o.shape[d];
+  }
+  return off;
+}
+
+template <typename T, int OP, bool KEYS>
+__global__ void scatter_init_kernel(const T* __restrict__ out, typename Acc<T, OP, KEYS>::A* acc,
+                                    int32_t* cnt, OutGeo o, bool include_self) {
+  using AT = Acc<T, OP, KEYS>;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < o.numel;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t off = out_offset(o, i);
+    // the accumulator is indexed by the out offset (same strides as out)
+    acc[off] = include_self ? AT::from(out[off]) : AT::identity();
+    if (cnt) cnt[off] = 0;
+  }
+}
+
+template <typename T> __device__ __forceinline__ T from_acc(float a) { return from_f<T>(a); }
+template <> __device__ __forceinline__ int32_t from_acc<int32_t>(float a) { return (int32_t)a; }
+
+template <typename T, int OP, bool KEYS>
+__global__ void scatter_finalize_kernel(T* __restrict__ out,
+                                        const typename Acc<T, OP, KEYS>::A* __restrict__ acc,
+                                        const int32_t* __restrict__ cnt, OutGeo o,
+                                        bool include_self, bool acc_is_out) {
+  using AT = Acc<T, OP, KEYS>;
+  using A = typename AT::A;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < o.numel;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t off = out_offset(o, i);
+    if constexpr (KEYS) {
+      const uint32_t k = (uint32_t)acc[off];
+      if (!include_self && k == (uint32_t)AT::identity()) continue;  // never reached
+      out[off] = from_f<T>(funkey(k));
+      continue;
+    } else {
+    const int32_t c = cnt ? cnt[off] : 1;
+    if (!include_self && c == 0) continue;  // never reached: keeps self
+    A a = acc_is_out ? (A)0 : acc[off];
+    if (OP == kMean) {
+      const int32_t den = include_self ? c + 1 : c;
+      if constexpr (std::is_same<A, float>::value) {
+        const float s = acc_is_out ? tof<T>(out[off]) : a;
+        out[off] = from_f<T>(s / (float)den);
+      } else {
+        const A s = acc_is_out ? (A)reinterpret_cast<const A*>(out)[off] : a;
+        A q = s / (A)den;
+        if ((s % (A)den != 0) && ((s < 0) != (den < 0))) q -= 1;  // floor division
+        reinterpret_cast<A*>(out)[off] = q;
+      }
+    } else if (!acc_is_out) {
+      if constexpr (std::is_same<A, float>::value) out[off] = from_f<T>(a);
+      else reinterpret_cast<A*>(out)[off] = a;
+    }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// planning + dispatch
+// ---------------------------------------------------------------------------
+inline bool is_float(int dt) { return dt == FO_F32 || dt == FO_F16 || dt == FO_BF16; }
+inline size_t round256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+struct Plan {
+  bool keys;     // float amax/amin via uint32 keys in scratch
+  bool scratch;  // accumulator in scratch (else directly in out)
+  bool counts;   // int32 counts in scratch
+  size_t acc_bytes, cnt_bytes;
+};
+
+Plan make_plan(int reduce, bool include_self, int dtype, int64_t span) {
+  Plan p{};
+  const bool f = is_float(dtype);
+  const bool half = dtype == FO_F16 || dtype == FO_BF16;
+  p.keys = f && (reduce == FO_AMAX || reduce == FO_AMIN);
+  p.counts = (reduce == FO_MEAN) || (!include_self && !p.keys);
+  p.scratch = p.keys || !include_self || half;
+  size_t asz = p.keys ? 4 : (f ? 4 : dtype_size(dtype));
+  p.acc_bytes = p.scratch ? round256((size_t)span * asz) : 0;
+  p.cnt_bytes = p.counts ? round256((size_t)span * 4) : 0;
+  return p;
+}
+
+// number of elements an out-offset-indexed array must cover
+int64_t out_span(const int64_t* shape, const int64_t* str, int ndim) {
+  int64_t m = 0;
+  for (int d = 0; d < ndim; ++d) {
+    if (shape[d] == 0) return 0;
+    m += (shape[d] - 1) * str[d];
+  }
+  return m + 1;
+}
+
+template <typename T, typename I, int OP, bool KEYS>
+int run(void* out, const void* src, const void* index, const Geo& g, const OutGeo& og,
+        int64_t n, bool include_self, const Plan& pl, void* ws, int32_t* err, cudaStream_t st) {
+  using AT = Acc<T, OP, KEYS>;
+  using A = typename AT::A;
+  A* acc = pl.scratch ? reinterpret_cast<A*>(ws) : reinterpret_cast<A*>(out);
+  int32_t* cnt = pl.counts ? reinterpret_cast<int32_t*>((char*)ws + pl.acc_bytes) : nullptr;
+  const int sms = num_sms();
+  if (pl.scratch) {
+    int64_t gi = (og.numel + 255) / 256;
+    if (gi > sms * 8) gi = sms * 8;
+    if (gi < 1) gi = 1;
+    scatter_init_kernel<T, OP, KEYS><<<(unsigned)gi, 256, 0, st>>>((const T*)out, acc, cnt, og,
+                                                                    include_self);
+    if (int rc = check_launch("scatter_init_kernel")) return rc;
+  } else if (cnt) {
+    cudaMemsetAsync(cnt, 0, pl.cnt_bytes, st);
+  }
+  if (n > 0) {
+    const int64_t span = out_span(og.shape, og.str, og.ndim);
+    const bool use_cache = span < (int64_t)0xffffffffLL;
+    int64_t grid = (n + (int64_t)kThreads * 16 - 1) / ((int64_t)kThreads * 16);
+    if (grid > (int64_t)sms * 2) grid = (int64_t)sms * 2;
+    if (grid < 1) grid = 1;
+    const bool vec = g.ndim == 1 && sizeof(I) == 8 && g.istr[0] == 1 && g.sstr[0] == 1 &&
+                     aligned16(index) && aligned16(src);
+#define FO_LAUNCH(ND, V)                                                                       \
+  scatter_kernel<T, I, OP, KEYS, true, ND, V><<<(unsigned)grid, kThreads, 0, st>>>(            \
+      (const T*)src, (const I*)index, acc, cnt, n, g, err, use_cache)
+#define FO_LAUNCH_NC(ND, V)                                                                    \
+  scatter_kernel<T, I, OP, KEYS, false, ND, V><<<(unsigned)grid, kThreads, 0, st>>>(           \
+      (const T*)src, (const I*)index, acc, nullptr, n, g, err, use_cache)
+    if (cnt) {
+      if (vec) FO_LAUNCH(1, (sizeof(I) == 8));
+      else if (g.ndim == 1) FO_LAUNCH(1, false);
+      else if (g.ndim == 2) FO_LAUNCH(2, false);
+      else if (g.ndim == 3) FO_LAUNCH(3, false);
+      else FO_LAUNCH(4, false);
+    } else {
+      if (vec) FO_LAUNCH_NC(1, (sizeof(I) == 8));
+      else if (g.ndim == 1) FO_LAUNCH_NC(1, false);
+      else if (g.ndim == 2) FO_LAUNCH_NC(2, false);
+      else if (g.ndim == 3) FO_LAUNCH_NC(3, false);
+      else FO_LAUNCH_NC(4, false);
+    }
+#undef FO_LAUNCH
+#undef FO_LAUNCH_NC
+    if (int rc = check_launch("scatter_kernel")) return rc;
+  }
+  if (pl.scratch || OP == kMean) {
+    int64_t gf = (og.numel + 255) / 256;
+    if (gf > sms * 8) gf = sms * 8;
+    if (gf < 1) gf = 1;
+    scatter_finalize_kernel<T, OP, KEYS><<<(unsigned)gf, 256, 0, st>>>(
+        (T*)out, acc, cnt, og, include_self, !pl.scratch);
+    if (int rc = check_launch("scatter_finalize_kernel")) return rc;
+  }
+  return FO_OK;
+}
+
+template <typename T, typename I>
+int dispatch_op(int reduce, void* out, const void* src, const void* index, const Geo& g,
+                const OutGeo& og, int64_t n, bool inc, const Plan& pl, void* ws, int32_t* err,
+                cudaStream_t st) {
+  constexpr bool F = std::is_same<T, float>::value || std::is_same<T, __half>::value ||
+                     std::is_same<T, __nv_bfloat16>::value;
+  switch (reduce) {
+    case FO_SUM: return run<T, I, kSum, false>(out, src, index, g, og, n, inc, pl, ws, err, st);
+    case FO_PROD: return run<T, I, kProd, false>(out, src, index, g, og, n, inc, pl, ws, err, st);
+    case FO_MEAN: return run<T, I, kMean, false>(out, src, index, g, og, n, inc, pl, ws, err, st);
+    case FO_AMAX: return run<T, I, kAmax, F>(out, src, index, g, og, n, inc, pl, ws, err, st);
+    case FO_AMIN: return run<T, I, kAmin, F>(out, src, index, g, og, n, inc, pl, ws, err, st);
+  }
+  set_error("scatter_reduce: Unsupported reduce code %d", reduce);
+  return FO_EINVAL;
+}
+
+template <typename I>
+int dispatch_dtype(int dtype, int reduce, void* out, const void* src, const void* index,
+                   const Geo& g, const OutGeo& og, int64_t n, bool inc, const Plan& pl, void* ws,
+                   int32_t* err, cudaStream_t st) {
+  switch (dtype) {
+    case FO_F32: return dispatch_op<float, I>(reduce, out, src, index, g, og, n, inc, pl, ws, err, st);
+    case FO_F16: return dispatch_op<__half, I>(reduce, out, src, index, g, og, n, inc, pl, ws, err, st);
+    case FO_BF16:
+      return dispatch_op<__nv_bfloat16, I>(reduce, out, src, index, g, og, n, inc, pl, ws, err, st);
+    case FO_I32: return dispatch_op<int32_t, I>(reduce, out, src, index, g, og, n, inc, pl, ws, err, st);
+    case FO_I64: return dispatch_op<int64_t, I>(reduce, out, src, index, g, og, n, inc, pl, ws, err, st);
+  }
+  set_error("scatter_reduce: unsupported dtype code %d", dtype);
+  return FO_EDTYPE;
+}
+
+}  // namespace
+}  // namespace fo
+
+using namespace fo;
+
+extern "C" int fo_scatter_reduce_workspace_bytes(int64_t out_numel, int reduce, int include_self,
+                                                 int dtype, int64_t* bytes) {
+  clear_error();
+  FO_CHECK_ARG(bytes && out_numel >= 0, "fo_scatter_reduce_workspace_bytes: bad argument");
+  FO_CHECK_ARG(reduce >= FO_SUM && reduce <= FO_AMIN, "Unsupported reduce code %d", reduce);
+  const Plan p = make_plan(reduce, include_self != 0, dtype, out_numel);
+  *bytes = (int64_t)(p.acc_bytes + p.cnt_bytes);
+  return FO_OK;
+}
+
+extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, int ndim,
+                                 const int64_t* index_shape, const int64_t* index_strides,
+                                 const int64_t* src_strides, const int64_t* out_shape,
+                                 const int64_t* out_strides, int dim, int reduce,
+                                 int include_self, int dtype, int index_dtype, void* workspace,
+                                 int64_t ws_bytes, int32_t* err_count, void* stream) {
+  clear_error();
+  FO_CHECK_ARG(ndim >= 1 && ndim <= 4, "scatter_reduce supports 1-4-D tensors, got %dD", ndim);
+  FO_CHECK_ARG(dim >= 0 && dim < ndim, "scatter_reduce: dim %d out of range", dim);
+  FO_CHECK_ARG(reduce >= FO_SUM && reduce <= FO_AMIN, "Unsupported reduce code %d", reduce);
+  FO_CHECK_ARG(index_dtype == FO_I64 || index_dtype == FO_I32,
+               "scatter_reduce: index must be int64 or int32");
+  FO_CHECK_ARG(index_shape && index_strides && src_strides && out_shape && out_strides,
+               "scatter_reduce: null shape/stride array");
+  Geo g{};
+  OutGeo og{};
+  int64_t n = 1;
+  og.numel = 1;
+  for (int d = 0; d < 4; ++d) {
+    g.shape[d] = d < ndim ? index_shape[d] : 1;
+    g.istr[d] = d < ndim ? index_strides[d] : 0;
+    g.sstr[d] = d < ndim ? src_strides[d] : 0;
+    g.ostr[d] = d < ndim ? out_strides[d] : 0;
+    og.shape[d] = d < ndim ? out_shape[d] : 1;
+    og.str[d] = d < ndim ? out_strides[d] : 0;
+    FO_CHECK_ARG(g.shape[d] >= 0 && og.shape[d] >= 0, "scatter_reduce: negative shape");
+    n *= g.shape[d];
+    og.numel *= og.shape[d];
+  }
+  for (int d = 0; d < ndim; ++d)
+    FO_CHECK_ARG(d == dim || index_shape[d] <= out_shape[d],
+                 "scatter_reduce: index size %lld > self size %lld at dim %d",
+                 (long long)index_shape[d], (long long)out_shape[d], d);
+  g.out_dim = out_shape[dim];
+  g.dim = dim;
+  g.ndim = ndim;
+  og.ndim = ndim;
+  if (og.numel == 0) return FO_OK;
+  FO_CHECK_ARG(out && (n == 0 || (src && index)), "scatter_reduce: null pointer");
+  const int64_t span = out_span(og.shape, og.str, ndim);
+  const Plan pl = make_plan(reduce, include_self != 0, dtype, span);
+  if ((int64_t)(pl.acc_bytes + pl.cnt_bytes) > 0 &&
+      (!workspace || ws_bytes < (int64_t)(pl.acc_bytes + pl.cnt_bytes))) {
+    set_error("scatter_reduce: workspace of %lld bytes required, got %lld",
+              (long long)(pl.acc_bytes + pl.cnt_bytes), (long long)ws_bytes);
+    return FO_EWORKSPACE;
+  }
+  cudaStream_t st = as_stream(stream);
+  if (index_dtype == FO_I64)
+    return dispatch_dtype<int64_t>(dtype, reduce, out, src, index, g, og, n, include_self != 0, pl,
+                                   workspace, err_count, st);
+  return dispatch_dtype<int32_t>(dtype, reduce, out, src, index, g, og, n, include_self != 0, pl,
+                                 workspace, err_count, st);
+}

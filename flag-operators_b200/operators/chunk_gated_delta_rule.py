@@ -1,0 +1,103 @@
+"""chunk_gated_delta_rule — drop-in for operators/chunk_gated_delta_rule.py of Flag-Operators.
+
+    chunk_gated_delta_rule(q, k, v, beta, g) -> o
+    h_t = g_t h_{t-1} + beta_t (v_t - h_{t-1} k_t) k_t^T ,  o_t = h_t q_t
+
+q, k, v: [B, H, L, D] with D in {16, 32, 64, 128}; beta, g: [B, H, L]; o has q's
+dtype, the state is fp32 (as the reference, chunk_gated_delta_rule.py:208-268).
+Keyword-only extensions (defaults keep the reference behaviour):
+  initial_state=None   fp32 [B, H, D, D] state before the first token
+  output_final_state=False   also return the fp32 final state: (o, h_T)
+
+Kernels: D = 128 with bf16/fp16 inputs runs the chunked tensor-core kernel
+(csrc/delta_rule_tc.cu: chunks of 64 tokens, seven tcgen05 GEMMs per chunk,
+fp32 state in TMEM); other shapes run the per-step kernel
+(csrc/delta_rule_step.cu).  _ref_forward is kept importable, as the reference's
+tests import it; it is the reference's sequential fp32 loop on CPU tensors.
+"""
+from __future__ import annotations
+
+import logging
+
+import torch
+
+from . import _lib
+
+logger = logging.getLogger(__name__)
+
+
+def _check_inputs(q, k, v, beta, g):
+    """The reference's shape checks (chunk_gated_delta_rule.py:198-205)."""
+    B, H, L, D = q.shape
+    assert k.shape == q.shape, f"k shape {k.shape} != q shape {q.shape}"
+    assert v.shape == q.shape, f"v shape {v.shape} != q shape {q.shape}"
+    assert beta.shape == (B, H, L), f"beta shape {beta.shape}, expected ({B},{H},{L})"
+    assert g.shape == (B, H, L), f"g shape {g.shape}, expected ({B},{H},{L})"
+    assert D in (16, 32, 64, 128), f"D={D} not in supported set {{16,32,64,128}}"
+    return B, H, L, D
+
+
+def chunk_gated_delta_rule(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    beta: torch.Tensor,
+    g: torch.Tensor,
+    *,
+    initial_state: torch.Tensor | None = None,
+    output_final_state: bool = False,
+):
+    """Gated delta rule forward (chunk_gated_delta_rule.py:208-268)."""
+    logger.debug("FLAG-OPS CHUNK_GATED_DELTA_RULE")
+    _lib.require_cuda(q, "chunk_gated_delta_rule")
+    B, H, L, D = _check_inputs(q, k, v, beta, g)
+    if not (k.dtype == q.dtype and v.dtype == q.dtype):
+        raise TypeError("chunk_gated_delta_rule: q, k and v must share a dtype")
+    if beta.dtype != g.dtype:
+        g = g.to(beta.dtype)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    beta, g = beta.contiguous(), g.contiguous()
+    o = torch.empty_like(q)
+    h0 = None
+    if initial_state is not None:
+        assert initial_state.shape == (B, H, D, D), (
+            f"initial_state shape {tuple(initial_state.shape)}, expected ({B},{H},{D},{D})")
+        h0 = initial_state.to(device=q.device, dtype=torch.float32).contiguous()
+    hT = torch.empty(B, H, D, D, dtype=torch.float32, device=q.device) \
+        if output_final_state else None
+    _lib.call("fo_gdr_fwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(beta), _lib.ptr(g),
+              _lib.ptr(h0), _lib.ptr(o), _lib.ptr(hT), B, H, L, D, _lib.dtype_code(q.dtype),
+              _lib.dtype_code(beta.dtype), _lib.stream_of(q))
+    if output_final_state:
+        return o, hT
+    return o
+
+
+def _ref_forward(q, k, v, beta, g):
+    """The reference's sequential loop (chunk_gated_delta_rule.py:275-310), CPU/any device.
+
+    Kept because the reference's tests import it; it is not used by the kernels.
+    """
+    B, H, L, D = q.shape
+    dtype = q.dtype
+    h = torch.zeros(B, H, D, D, dtype=torch.float32, device=q.device)
+    o = torch.empty_like(q)
+    for t in range(L):
+        q_t = q[:, :, t, :].float()
+        k_t = k[:, :, t, :].float()
+        v_t = v[:, :, t, :].float()
+        beta_t = beta[:, :, t]
+        g_t = g[:, :, t]
+        residual = (h @ k_t.unsqueeze(-1)).squeeze(-1)
+        delta = v_t - residual
+        h = (g_t[:, :, None, None] * h
+             + beta_t[:, :, None, None] * (delta.unsqueeze(-1) * k_t.unsqueeze(-2)))
+        o[:, :, t, :] = (h @ q_t.unsqueeze(-1)).squeeze(-1).to(dtype)
+    return o
+
+
+def timeouts() -> int:
+    """Tensor-core waits that ran out of polls since load (0 in a healthy run)."""
+    c = _lib.ctypes.c_uint(0)
+    _lib.call("fo_gdr_timeouts", _lib.ctypes.byref(c))
+    return int(c.value)

@@ -228,6 +228,18 @@ FO_API int fo_gdr_fwd_stepwise(const void* q, const void* k, const void* v,
                         void* o, float* hT, int64_t B, int64_t H, int64_t L,
                         int64_t D, int dtype, int gate_dtype, void* stream);
 
+/* Number of tensor-core waits of the chunked kernel that ran out of polls since
+ * the library was loaded (0 in a healthy run; a timed-out head leaves its
+ * outputs incomplete).  Synchronous read of a device counter. */
+FO_API int fo_gdr_timeouts(unsigned int* count);
+
+/* Operand-layout self-test of the tensor-core path (no reference counterpart):
+ * d[128, N] (fp32) = A[128, K] . B[N, K]^T on one CTA with tcgen05.mma, bf16 A/B.
+ * a is [128][K] (a_mn = 0, K-major) or [K][128] (a_mn = 1); b is [N][K] (b_mn = 0)
+ * or [K][N] (b_mn = 1).  N, K in {64, 128}. */
+FO_API int fo_tc05_selftest(const void* a, const void* b, float* d, int64_t N, int64_t K,
+                            int a_mn, int b_mn, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

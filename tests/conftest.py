@@ -35,9 +35,8 @@ def load_golden(name: str) -> dict:
         a = z[k]
         if k.endswith("__bf16"):
             out[k[:-6]] = torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
-        elif a.ndim == 0 and a.dtype.kind in "fiub":
-            out[k] = a.item()
-            out[k + "__t"] = torch.from_numpy(np.array(a))
+        elif k.endswith("__s"):
+            out[k[:-3]] = a.item()
         else:
             out[k] = torch.from_numpy(a.copy())
     return out

@@ -37,7 +37,7 @@ def _save(name: str, **tensors):
             arr, suf = _np(v)
             out[k + suf] = arr
         else:
-            out[k] = np.asarray(v)
+            out[k + "__s"] = np.asarray(v)   # plain scalar parameter
     path = os.path.join(HERE, name + ".npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({os.path.getsize(path)} bytes)")
