@@ -7,35 +7,47 @@
 // one fp32 ulp before the final rounding.
 //
 // Design: a row is read from HBM exactly once.  A CTA owns whole rows; every
-// thread keeps VPT 16-byte vectors of the row in registers, the row's sum of
-// squares is a block reduction, then the same registers are scaled and stored.
-// CTAs are persistent over rows (grid-stride), so the weight slice each thread
-// needs is loaded into registers once per CTA, not once per row.
+// thread keeps VPT 16-byte vectors of the row in registers (VPT = 2 and 512
+// threads for rows of 16 KiB), the row's sum of squares is a block reduction,
+// then the same registers are scaled and stored.  CTAs are persistent over rows
+// (grid-stride), so the weight slice each thread needs is loaded into registers
+// once per CTA, not once per row.
 #include "common.cuh"
 
 namespace fo {
 namespace {
 
 template <typename T, typename W, int VPT>
-__global__ void __launch_bounds__(512)
+__global__ void __launch_bounds__(512, VPT <= 2 ? 2 : 1)
 rms_fwd_vec_kernel(const T* __restrict__ x, const W* __restrict__ w, T* __restrict__ y,
                    float* __restrict__ inv_rms, int64_t M, int N, float eps) {
   constexpr int E = Vec16<T>::E;
-  // Long rows keep only x in registers; the weight is then re-read (L1 hit).
-  constexpr bool kCacheW = VPT <= 4;
-  constexpr int WV = kCacheW ? VPT : 1;
+  // The weight slice of a thread is cached packed (16 bytes of W per 16 bytes of
+  // x when the dtypes match) and unpacked at use, keeping the register count low
+  // enough for 4 CTAs of 512 threads per SM.
+  constexpr int WB = E * (int)sizeof(W);        // weight bytes per x vector
+  constexpr int WV = (WB + 15) / 16;            // 16-byte words per x vector
   __shared__ float red[32];
   const int nvec = N / E;
 
-  float wf[WV][E];
-  if (kCacheW) {
+  uint4 wr[VPT][WV];
 #pragma unroll
-    for (int i = 0; i < WV; ++i) {
-      const int v = threadIdx.x + i * blockDim.x;
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
 #pragma unroll
-      for (int e = 0; e < E; ++e) wf[i][e] = (v < nvec) ? to_f<W>(w[(int64_t)v * E + e]) : 0.f;
+    for (int u = 0; u < WV; ++u) {
+      if (v < nvec && WB % 16 == 0) wr[i][u] = *reinterpret_cast<const uint4*>(
+          reinterpret_cast<const uint8_t*>(w) + (int64_t)v * WB + u * 16);
+      else wr[i][u] = make_uint4(0, 0, 0, 0);
     }
   }
+  auto weight = [&](int i, int e, int v) -> float {
+    if constexpr (WB % 16 == 0) {
+      return to_f<W>(reinterpret_cast<const W*>(&wr[i][0])[e]);
+    } else {
+      return to_f<W>(w[(int64_t)v * E + e]);
+    }
+  };
 
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const T* xr = x + row * (int64_t)N;
@@ -66,10 +78,7 @@ rms_fwd_vec_kernel(const T* __restrict__ x, const W* __restrict__ w, T* __restri
         float f[E];
         unpack16<T>(raw[i], f);
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const float we = kCacheW ? wf[kCacheW ? i : 0][e] : to_f<W>(w[(int64_t)v * E + e]);
-          f[e] = (f[e] * inv) * we;
-        }
+        for (int e = 0; e < E; ++e) f[e] = (f[e] * inv) * weight(i, e, v);
         st_global_stream_v4(yr + (int64_t)v * E, pack16<T>(f));
       }
     }
@@ -124,8 +133,8 @@ int launch(const void* x, const void* w, void* y, float* inv_rms, int64_t M, int
   const bool vec_ok = aligned16(x) && aligned16(y) && (N % E == 0) && N <= (int64_t)512 * 8 * E;
   if (vec_ok) {
     const int nvec = (int)(N / E);
-    if (nvec <= 256) return launch_vec<T, W, 1>(x, w, y, inv_rms, M, (int)N, eps, st);
-    if (nvec <= 512) return launch_vec<T, W, 2>(x, w, y, inv_rms, M, (int)N, eps, st);
+    if (nvec <= 512) return launch_vec<T, W, 1>(x, w, y, inv_rms, M, (int)N, eps, st);
+    if (nvec <= 1024) return launch_vec<T, W, 2>(x, w, y, inv_rms, M, (int)N, eps, st);
     if (nvec <= 2048) return launch_vec<T, W, 4>(x, w, y, inv_rms, M, (int)N, eps, st);
     return launch_vec<T, W, 8>(x, w, y, inv_rms, M, (int)N, eps, st);
   }
