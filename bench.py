@@ -150,13 +150,20 @@ def delta_flops(B=8, H=16, L=8192, D=128, C=64):
 # timing helpers
 # ---------------------------------------------------------------------------
 class Flusher:
-    """Writes a buffer larger than L2 (126 MB) to evict the inputs between steps."""
+    """Evicts the inputs from L2 (126 MB) between steps: writes a 256 MiB buffer,
+    then reads a second 256 MiB buffer, so the dirty lines of the write are
+    written back here, outside the timed region, and L2 ends full of clean lines
+    of neither the inputs nor the outputs."""
 
     def __init__(self, dev):
-        self.buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+        n = 256 * 1024 * 1024 // 4
+        self.wbuf = torch.empty(n, dtype=torch.float32, device=dev)
+        self.rbuf = torch.ones(n, dtype=torch.float32, device=dev)
+        self.sink = torch.empty((), dtype=torch.float32, device=dev)
 
     def __call__(self):
-        self.buf.fill_(1.0)
+        self.wbuf.fill_(1.0)
+        torch.sum(self.rbuf, dim=0, out=self.sink)
 
 
 def time_steps(fn, steps, warmup, flush=None, dist=None):

@@ -60,13 +60,12 @@ constexpr uint32_t OFF_KT = 49152;     // 2 x [64 x 128B]  Kt
 constexpr uint32_t OFF_T = 65536;      // [64 x 128B]      T
 constexpr uint32_t OFF_P = 73728;      // [64 x 128B]      P
 constexpr uint32_t OFF_WT = 81920;     // [128 x 128B]     -W^T
-constexpr uint32_t OFF_S = 98304;      // 2 x [128 x 128B] state (bf16)
-constexpr uint32_t OFF_UT = 131072;    // [128 x 128B]     U^T
-constexpr uint32_t OFF_O = 147456;     // [64 x 256B]      output staging (row-major)
-constexpr uint32_t OFF_A = 163840;     // fp32 [64][65]    A
-constexpr uint32_t OFF_TI = 180480;    // fp32 [64][65]    T (fp32)
-constexpr uint32_t OFF_X = 197120;     // fp32 [3][16][16] blocked-inverse scratch
-constexpr uint32_t OFF_G = 200192;     // gate tables
+constexpr uint32_t OFF_S = 98304;      // 2 x [128 x 128B] state (fp16 copy)
+constexpr uint32_t OFF_UT = 131072;    // [128 x 128B]     U^T; then output staging [64 x 256B]
+constexpr uint32_t OFF_RAW = 147456;   // [3][64 x 256B]   next chunk's q, k, v rows (bulk copy)
+constexpr uint32_t OFF_A = 196608;     // fp32 [64][68]    A (rows 16-byte aligned)
+constexpr uint32_t OFF_G = 214016;     // gate tables + barriers
+constexpr int kAStride = 68;
 constexpr uint32_t G_LC = 0, G_Z = 256, G_NEG = 512, G_BETA = 768, G_GAM = 1024, G_GAMP = 1280,
                    G_KTS = 1536, G_MISC = 1792;
 constexpr uint32_t kSmemBytes = OFF_G + 2048 + 1024;  // + alignment slack
@@ -148,12 +147,11 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   float* sGamP = reinterpret_cast<float*>(sm + OFF_G + G_GAMP);
   float* sKts = reinterpret_cast<float*>(sm + OFF_G + G_KTS);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + OFF_G + G_MISC);
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_G + G_MISC + 8);
-  int* s_abort = reinterpret_cast<int*>(sm + OFF_G + G_MISC + 12);
-  float* s_gc = reinterpret_cast<float*>(sm + OFF_G + G_MISC + 16);
+  uint64_t* rawbar = reinterpret_cast<uint64_t*>(sm + OFF_G + G_MISC + 8);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_G + G_MISC + 16);
+  int* s_abort = reinterpret_cast<int*>(sm + OFF_G + G_MISC + 20);
+  float* s_gc = reinterpret_cast<float*>(sm + OFF_G + G_MISC + 24);
   float* sA = reinterpret_cast<float*>(sm + OFF_A);
-  float* sTi = reinterpret_cast<float*>(sm + OFF_TI);
-  float* sX = reinterpret_cast<float*>(sm + OFF_X);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int quad = warp & 3, colh = warp >> 2;
@@ -166,6 +164,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   const G* gh = g + head * L;
   constexpr bool BF = false;  // operands are fp16
   const GateTabs gt{sLc, sZ, sNeg};
+  const int64_t nchunks = (L + kC - 1) / kC;
 
   if (warp == 0) {
     tc::tmem_alloc(s_tmem, TM_COLS);
@@ -173,6 +172,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   }
   if (tid == 0) {
     tc::mbar_init(mbar, 1);
+    tc::mbar_init(rawbar, 1);
     tc::fence_mbar_init();
     *s_abort = 0;
   }
@@ -181,21 +181,33 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   tc::fence_after_sync();
   const uint32_t tm = *s_tmem;
   const uint32_t tm_lane = tm + ((uint32_t)(32 * quad) << 16);
-  uint32_t phase = 0;
+  uint32_t phase = 0, rphase = 0;
   bool state_nz = false;
 
-  // MMA completion: thread 0 polls the mbarrier (bounded) and the CTA barrier
-  // publishes the result, so every thread takes the same branch on abort.
-  auto mma_wait = [&]() {
+  // q, k, v rows of chunk c -> RAW (bulk copies, completion on rawbar)
+  auto issue_raw = [&](int64_t c) {
+    const int64_t t0 = c * kC;
+    const int nv = (int)((L - t0) < kC ? (L - t0) : kC);
+    const uint32_t bytes = (uint32_t)nv * kD * sizeof(T);
+    tc::mbar_arrive_expect_tx(rawbar, 3 * bytes);
+    tc::bulk_g2s(sm + OFF_RAW, qh + t0 * kD, bytes, rawbar);
+    tc::bulk_g2s(sm + OFF_RAW + 16384, kh + t0 * kD, bytes, rawbar);
+    tc::bulk_g2s(sm + OFF_RAW + 32768, vh + t0 * kD, bytes, rawbar);
+  };
+  // thread 0 polls an mbarrier (bounded); the CTA barrier publishes the outcome
+  auto bar_wait = [&](uint64_t* bar, uint32_t& ph) {
     if (tid == 0) {
-      if (!tc::mbar_wait(mbar, phase, kWaitLimit)) {
+      if (!tc::mbar_wait(bar, ph, kWaitLimit)) {
         atomicAdd(&g_gdr_timeouts, 1u);
         *s_abort = 1;
       }
     }
-    phase ^= 1u;
+    ph ^= 1u;
     cta_sync_tc();
   };
+  auto mma_wait = [&]() { bar_wait(mbar, phase); };
+
+  if (tid == 0 && nchunks > 0) issue_raw(0);
 
   // ---- initial state
   if (h0) {
@@ -208,7 +220,6 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
 #pragma unroll
       for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(hh[i * kD + j0 + j]);
       tc::tmem_st32(tm_lane + TM_S + j0, r);
-      // bf16 copy: half `colh` of the state, chunks (32*half)/8 ..
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint4 pk;
@@ -224,24 +235,11 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
     state_nz = true;
   }
 
-  const int64_t nchunks = (L + kC - 1) / kC;
   for (int64_t c = 0; c < nchunks; ++c) {
     const int64_t tok0 = c * kC;
     const int nvalid = (int)((L - tok0) < kC ? (L - tok0) : kC);
 
-    // ---- load q, k, v rows of the chunk into swizzled tiles; gates to smem
-    for (int idx = tid; idx < 3 * 1024; idx += kThr) {
-      const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
-      const int half = ch >> 3, cc = ch & 7;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      const T* srcp = (m == 0) ? qh : (m == 1 ? kh : vh);
-      if (t < nvalid) val = to_op8<T>(ld_global_stream_v4(srcp + (tok0 + t) * kD + ch * 8));
-      uint32_t off;
-      if (m == 0) off = OFF_QK + half * 16384 + tc::sw128_chunk(t, cc);
-      else if (m == 1) off = OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc);
-      else off = OFF_V + half * 8192 + tc::sw128_chunk(t, cc);
-      *reinterpret_cast<uint4*>(sm + off) = val;
-    }
+    // ---- gates (small direct loads) while the bulk copy lands
     if (tid < 64) {
       const bool ok = tid < nvalid;
       const float bt = ok ? to_f<G>(bh[tok0 + tid]) : 0.f;
@@ -266,13 +264,31 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       sZ[tid] = zi;
       sNeg[tid] = ng;
     }
-    __syncthreads();
+    bar_wait(rawbar, rphase);  // includes a CTA barrier
+    if (*s_abort) break;
     if (tid >= 32 && tid < 64) {
       sLc[tid] += sLc[31];
       sZ[tid] = max(sZ[tid], sZ[31]);
       sNeg[tid] += sNeg[31];
     }
+    // RAW (T, row-major) -> fp16 swizzled operand tiles; rows past the end are zero
+    for (int idx = tid; idx < 3 * 1024; idx += kThr) {
+      const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
+      const int half = ch >> 3, cc = ch & 7;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (t < nvalid)
+        val = to_op8<T>(*reinterpret_cast<const uint4*>(sm + OFF_RAW + m * 16384 + t * 256 + ch * 16));
+      uint32_t off;
+      if (m == 0) off = OFF_QK + half * 16384 + tc::sw128_chunk(t, cc);
+      else if (m == 1) off = OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc);
+      else off = OFF_V + half * 8192 + tc::sw128_chunk(t, cc);
+      *reinterpret_cast<uint4*>(sm + off) = val;
+    }
     __syncthreads();
+    if (tid == 0 && c + 1 < nchunks) {
+      tc::fence_proxy_async();  // RAW was read through the generic proxy
+      issue_raw(c + 1);
+    }
     if (tid < 64) {
       sGam[tid] = gt.ratio(tid, -1);
       sGamP[tid] = tid > 0 ? gt.ratio(tid - 1, -1) : 1.f;
@@ -325,91 +341,58 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int s = 32 * colh + j;
-          sA[t * 65 + s] = (s < t) ? gt.ratio(t - 1, s) * sBeta[s] * __uint_as_float(r[j]) : 0.f;
+          sA[t * kAStride + s] =
+              (s < t) ? gt.ratio(t - 1, s) * sBeta[s] * __uint_as_float(r[j]) : 0.f;
         }
-      }
-    }
-    // scaled copies: gQ (in place), Kt (new), gK (in place)
-    for (int idx = tid; idx < 2048; idx += kThr) {
-      const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
-      const int half = ch >> 3, cc = ch & 7;
-      if (m == 0) {
-        uint4* p = reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 + tc::sw128_chunk(t, cc));
-        *p = scale8<Op>(*p, sGam[t]);
-      } else {
-        uint4* p = reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc));
-        const uint4 raw = *p;
-        *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
-            scale8<Op>(raw, sKts[t]);
-        *p = scale8<Op>(raw, sGamP[t]);
       }
     }
     cta_sync_tc();
 
-    // ---- T = (I + A)^-1, blocked (16 x 16) forward substitution in fp32
-    if (warp < 4) {
-      const int b0 = 16 * warp, j = lane;
-      if (j < 16) {
-        for (int i = 0; i < 16; ++i) {
-          float val;
-          if (i < j) val = 0.f;
-          else if (i == j) val = 1.f;
-          else {
-            float acc = 0.f;
-            for (int m = j; m < i; ++m) acc = fmaf(sA[(b0 + i) * 65 + b0 + m], sTi[(b0 + m) * 65 + b0 + j], acc);
-            val = -acc;
-          }
-          sTi[(b0 + i) * 65 + b0 + j] = val;
+    if (tid < 64) {
+      // ---- T = (I + A)^-1 by forward substitution, one column per thread:
+      //      T[i][j] = [i == j] - sum_{m < i} A[i][m] T[m][j]
+      // The column lives in registers; row i of A is a broadcast read.
+      const int j = tid;
+      float col[kC];
+#pragma unroll
+      for (int i = 0; i < kC; ++i) {
+        float acc0 = (i == j) ? 1.f : 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+#pragma unroll
+        for (int m = 0; m < i; m += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(sA + i * kAStride + m);
+          acc0 = fmaf(-a4.x, col[m], acc0);
+          if (m + 1 < i) acc1 = fmaf(-a4.y, col[m + 1], acc1);
+          if (m + 2 < i) acc2 = fmaf(-a4.z, col[m + 2], acc2);
+          if (m + 3 < i) acc3 = fmaf(-a4.w, col[m + 3], acc3);
+        }
+        col[i] = (acc0 + acc1) + (acc2 + acc3);
+      }
+      // column j of T -> fp16 tile [t][s] (K-major B operand of (b), (c))
+      __half* tt = reinterpret_cast<__half*>(sm + OFF_T);
+#pragma unroll
+      for (int i = 0; i < kC; ++i)
+        *reinterpret_cast<__half*>(sm + OFF_T + tc::sw128_off(i, j)) = __float2half_rn(col[i]);
+      (void)tt;
+    } else {
+      // ---- scaled copies (other 6 warps): gQ (in place), Kt (new), gK (in place)
+      for (int idx = tid - 64; idx < 2048; idx += kThr - 64) {
+        const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
+        const int half = ch >> 3, cc = ch & 7;
+        if (m == 0) {
+          uint4* pp = reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 + tc::sw128_chunk(t, cc));
+          *pp = scale8<Op>(*pp, sGam[t]);
+        } else {
+          uint4* pp =
+              reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc));
+          const uint4 raw = *pp;
+          *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
+              scale8<Op>(raw, sKts[t]);
+          *pp = scale8<Op>(raw, sGamP[t]);
         }
       }
-    } else {
-      // zero the strictly upper 16x16 blocks
-      for (int e = tid - 128; e < 6 * 256; e += 128) {
-        const int blk = e >> 8, a = (e >> 4) & 15, bcol = e & 15;
-        const int I = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-        const int J = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-        sTi[(16 * I + a) * 65 + 16 * J + bcol] = 0.f;
-      }
-    }
-    __syncthreads();
-    for (int d = 1; d < 4; ++d) {
-      const int nblk = 4 - d;
-      for (int e = tid; e < nblk * 256; e += kThr) {
-        const int bi = e >> 8, a = (e >> 4) & 15, bcol = e & 15;
-        const int I = d + bi, J = bi;
-        float acc = 0.f;
-        for (int M = J; M < I; ++M)
-#pragma unroll
-          for (int m = 0; m < 16; ++m)
-            acc = fmaf(sA[(16 * I + a) * 65 + 16 * M + m], sTi[(16 * M + m) * 65 + 16 * J + bcol], acc);
-        sX[bi * 256 + a * 16 + bcol] = acc;
-      }
-      __syncthreads();
-      for (int e = tid; e < nblk * 256; e += kThr) {
-        const int bi = e >> 8, a = (e >> 4) & 15, bcol = e & 15;
-        const int I = d + bi, J = bi;
-        float acc = 0.f;
-#pragma unroll
-        for (int m = 0; m < 16; ++m)
-          acc = fmaf(sTi[(16 * I + a) * 65 + 16 * I + m], sX[bi * 256 + m * 16 + bcol], acc);
-        sTi[(16 * I + a) * 65 + 16 * J + bcol] = -acc;
-      }
-      __syncthreads();
-    }
-    // T -> bf16 K-major tile [t][s]
-    for (int e = tid; e < 512; e += kThr) {
-      const int t = e >> 3, ch = e & 7;
-      const float* src = sTi + t * 65 + ch * 8;
-      uint4 pk;
-      pk.x = pack2<Op>(src[0], src[1]);
-      pk.y = pack2<Op>(src[2], src[3]);
-      pk.z = pack2<Op>(src[4], src[5]);
-      pk.w = pack2<Op>(src[6], src[7]);
-      *reinterpret_cast<uint4*>(sm + OFF_T + tc::sw128_chunk(t, ch)) = pk;
     }
     tc::fence_proxy_async();
     cta_sync_tc();
-
     // ---- (b) W^T = (gK)^T T^T,  (c) U^T = V^T T^T
     if (tid == 0) {
       constexpr uint32_t id_mn = tc::idesc_f16(128, 64, BF, true, false);
@@ -521,7 +504,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       tc::tmem_ld32(tm_lane + TM_O + 32 * colh, r);
       tc::tmem_wait_ld();
       const int i = 32 * quad + lane;
-      T* so = reinterpret_cast<T*>(sm + OFF_O);
+      T* so = reinterpret_cast<T*>(sm + OFF_UT);
 #pragma unroll
       for (int j = 0; j < 32; ++j) so[(32 * colh + j) * kD + i] = from_f<T>(__uint_as_float(r[j]));
 #pragma unroll
@@ -545,10 +528,13 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
     for (int e = tid; e < nvalid * 16; e += kThr) {
       const int t = e >> 4, ch = e & 15;
       st_global_v4(oh + (tok0 + t) * kD + ch * 8,
-                   *reinterpret_cast<const uint4*>(sm + OFF_O + t * 256 + ch * 16));
+                   *reinterpret_cast<const uint4*>(sm + OFF_UT + t * 256 + ch * 16));
     }
     // (next chunk's loads overwrite QK/V/KT only after the barrier that follows them)
   }
+
+  // an abort can leave one bulk copy in flight: let it land before the CTA exits
+  if (*s_abort && tid == 0) tc::mbar_wait(rawbar, rphase, kWaitLimit);
 
   // ---- final state
   if (hT && !*s_abort) {

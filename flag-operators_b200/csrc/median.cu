@@ -71,37 +71,116 @@ template <typename K> struct Digits {
   static __device__ __forceinline__ int width(int p) { return kBits - 11 * p - shift(p); }
 };
 
-constexpr int kWarpHistWords = 1024;  // 2048 bins as packed 16-bit pairs
 
 // ---------------------------------------------------------------------------
-// warp per row
+// row groups of RG warps (N <= 2048): keys in registers, one radix pass,
+// compaction of the selected bucket, selection on the compacted list
 // ---------------------------------------------------------------------------
-// Lane `lane` holds, for i < NI and c < VW, the element at index
-// i * 32 * VW + lane * VW + c; index order is therefore (i, lane, c).
-template <typename T, int NI, int VW, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32)
-median_warp_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restrict__ idxs,
-                   int64_t M, int N) {
+// Element e of a row is held by warp w of the group, lane `lane`, slot (i, c):
+//   e = ((i * RG + w) * 32 + lane) * VW + c
+// (16-byte vectors when VW > 1).  The list holds composites
+//   (key << 32) | index
+// whose ascending order is the stable sort order, so the k-th composite is the
+// answer without a separate tie rule.
+template <int RG>
+__device__ __forceinline__ void group_sync(int g) {
+  if (RG == 1) __syncwarp();
+  else asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(RG * 32) : "memory");
+}
+
+// Per-row-group scratch: CAP = elements per row group (list capacity), HW =
+// histogram words (bins / 2, packed 16-bit counters).
+// The histogram comes first and the struct is 16-byte aligned: the histogram
+// is cleared with 16-byte stores (HW is a multiple of 4).
+template <int RG, int CAP, int HW>
+struct __align__(16) GroupSmem {
+  static_assert(HW % 4 == 0, "histogram words must be a multiple of 4");
+  uint32_t hist[HW];
+  unsigned long long list[CAP];
+  unsigned long long first_nan;
+  uint32_t wsum[RG];
+  uint32_t bucket, below, count, ncand;
+};
+
+// Finds the bin holding rank r among nbins bins (packed pairs in hist).
+// Returns (bin, #elements in lower bins, #elements in bin) to every thread.
+template <int RG, class GS>
+__device__ __forceinline__ void group_find(GS& S, int g, int nbins, uint32_t r,
+                                           uint32_t& bin, uint32_t& below, uint32_t& cnt) {
+  const int t = threadIdx.x & (RG * 32 - 1);
+  const int lane = t & 31, w = t >> 5;
+  const int per = (nbins >> 1) / (RG * 32);  // words per thread (>= 1)
+  const uint32_t* hw = S.hist + t * per;
+  uint32_t tot = 0;
+  for (int j = 0; j < per; ++j) tot += (hw[j] & 0xffffu) + (hw[j] >> 16);
+  uint32_t inc = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += x;
+  }
+  if (RG > 1) {
+    if (lane == 31) S.wsum[w] = inc;
+    group_sync<RG>(g);
+    uint32_t off = 0;
+    for (int q = 0; q < w; ++q) off += S.wsum[q];
+    inc += off;
+  }
+  const uint32_t exc = inc - tot;
+  if (exc <= r && r < inc) {
+    uint32_t acc = exc;
+    for (int j = 0; j < per; ++j) {
+      const uint32_t q = hw[j], c0 = q & 0xffffu, c1 = q >> 16;
+      if (r < acc + c0) { S.bucket = 2 * (t * per + j); S.below = acc; S.count = c0; break; }
+      acc += c0;
+      if (r < acc + c1) { S.bucket = 2 * (t * per + j) + 1; S.below = acc; S.count = c1; break; }
+      acc += c1;
+    }
+  }
+  group_sync<RG>(g);
+  bin = S.bucket;
+  below = S.below;
+  cnt = S.count;
+}
+
+template <int RG, class GS>
+__device__ __forceinline__ void group_clear_hist(GS& S, int nbins) {
+  const int t = threadIdx.x & (RG * 32 - 1);
+  for (int j = t * 4; j < (nbins >> 1); j += RG * 32 * 4)
+    *reinterpret_cast<uint4*>(S.hist + j) = make_uint4(0, 0, 0, 0);
+}
+
+__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t d) {
+  atomicAdd(hist + (d >> 1), 1u << ((d & 1u) << 4));
+}
+
+template <int RG, int NI, int VW, int DIG0, int DIGL>
+using GroupSmemOf = GroupSmem<RG, RG * 32 * NI * VW, (1 << (DIG0 > DIGL ? DIG0 : DIGL)) / 2>;
+
+template <typename T, int RG, int NI, int VW, int DIG0, int DIGL, int GPC>
+__global__ void __launch_bounds__(GPC * RG * 32)
+median_group_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restrict__ idxs,
+                    int64_t M, int N) {
   using Tr = KeyTraits<T>;
-  using K = typename Tr::K;
-  using D = Digits<K>;
-  __shared__ uint32_t hist_all[WARPS][kWarpHistWords];
-  const int lane = threadIdx.x & 31;
-  const int wid = threadIdx.x >> 5;
-  uint32_t* hist = hist_all[wid];
-  const int64_t gw = (int64_t)blockIdx.x * WARPS + wid;
-  const int64_t nwarps = (int64_t)gridDim.x * WARPS;
+  using GS = GroupSmemOf<RG, NI, VW, DIG0, DIGL>;
+  static_assert(sizeof(typename Tr::K) == 4, "32-bit keys only");
+  extern __shared__ __align__(16) uint8_t median_smem[];
+  const int g = threadIdx.x / (RG * 32);
+  const int t = threadIdx.x & (RG * 32 - 1);
+  const int lane = t & 31, w = t >> 5;
+  GS& S = reinterpret_cast<GS*>(median_smem)[g];
   const int k = (N - 1) / 2;
+  constexpr int SH0 = 32 - DIG0;
 
-  for (int64_t row = gw; row < M; row += nwarps) {
+  for (int64_t row = (int64_t)blockIdx.x * GPC + g; row < M; row += (int64_t)gridDim.x * GPC) {
     const T* xr = x + row * (int64_t)N;
-    K key[NI][VW];
+    uint32_t key[NI][VW];
     bool nan_seen = false;
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
-      const int base = i * 32 * VW + lane * VW;
+      const int base = ((i * RG + w) * 32 + lane) * VW;
       if (VW > 1 && base + VW <= N) {
-        uint4 u = ld_global_stream_v4(xr + base);
+        const uint4 u = ld_global_stream_v4(xr + base);
         const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
         for (int c = 0; c < VW; ++c) {
@@ -121,169 +200,134 @@ median_warp_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __res
         }
       }
     }
+    if (t == 0) {
+      S.first_nan = ~0ull;
+      S.ncand = 0;
+    }
+    group_clear_hist<RG>(S, 1 << DIG0);
+    group_sync<RG>(g);
 
-    int found_i = -1, found_c = 0, found_lane = 0;
-    if (__any_sync(0xffffffffu, nan_seen)) {
-      // first NaN in index order
-      for (int i = 0; i < NI && found_i < 0; ++i) {
-        int lane_c = VW;
-#pragma unroll
-        for (int c = VW - 1; c >= 0; --c) {
-          const int pos = i * 32 * VW + lane * VW + c;
-          if (pos < N && Tr::isnan_(xr[pos])) lane_c = c;
-        }
-        const uint32_t m = __ballot_sync(0xffffffffu, lane_c < VW);
-        if (m) {
-          found_lane = __ffs(m) - 1;
-          found_c = __shfl_sync(0xffffffffu, lane_c, found_lane);
-          found_i = i;
-        }
+    // ---- NaN: the first NaN in index order decides the row
+    const bool any_nan = (RG == 1) ? __any_sync(0xffffffffu, nan_seen) : false;
+    if (RG > 1 && nan_seen) atomicMin(&S.first_nan, 0ull);  // flag; resolved below
+    if (RG > 1) group_sync<RG>(g);
+    if ((RG == 1 && any_nan) || (RG > 1 && S.first_nan == 0ull)) {
+      if (RG > 1) {
+        group_sync<RG>(g);
+        if (t == 0) S.first_nan = ~0ull;
+        group_sync<RG>(g);
       }
-    } else {
-      K prefix = 0, pmask = 0;
-      int r = k;
-#pragma unroll 1
-      for (int p = 0; p < D::kPasses; ++p) {
-        const int sh = D::shift(p);
-        const int w = D::width(p);
-        const uint32_t dmask = (1u << w) - 1u;
-        const int words = (1 << w) >> 1;
-        for (int j = lane * 4; j < words; j += 128)
-          *reinterpret_cast<uint4*>(hist + j) = make_uint4(0, 0, 0, 0);
-        __syncwarp();
+      unsigned long long mine = ~0ull;
 #pragma unroll
-        for (int i = 0; i < NI; ++i) {
-#pragma unroll
-          for (int c = 0; c < VW; ++c) {
-            const int pos = i * 32 * VW + lane * VW + c;
-            const bool mine = pos < N && (key[i][c] & pmask) == prefix;
-            if (p == 0) {
-              if (mine) {
-                const uint32_t d = (uint32_t)(key[i][c] >> sh) & dmask;
-                atomicAdd(hist + (d >> 1), 1u << ((d & 1u) << 4));
-              }
-            } else if (__any_sync(0xffffffffu, mine)) {
-              if (mine) {
-                const uint32_t d = (uint32_t)(key[i][c] >> sh) & dmask;
-                atomicAdd(hist + (d >> 1), 1u << ((d & 1u) << 4));
-              }
-            }
-          }
-        }
-        __syncwarp();
-        // bucket holding rank r: lane sums its 1/32 slice of the words
-        const int per = words >> 5;  // words per lane (>= 16 when w >= 10)
-        uint32_t tot = 0;
-        for (int j = 0; j < per; j += 4) {
-          const uint4 q = *reinterpret_cast<const uint4*>(hist + lane * per + j);
-          tot += (q.x & 0xffffu) + (q.x >> 16) + (q.y & 0xffffu) + (q.y >> 16) + (q.z & 0xffffu) +
-                 (q.z >> 16) + (q.w & 0xffffu) + (q.w >> 16);
-        }
-        uint32_t inc = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
-          if (lane >= o) inc += t;
-        }
-        const uint32_t exc = inc - tot;
-        const uint32_t sel = __ballot_sync(0xffffffffu, exc <= (uint32_t)r && (uint32_t)r < inc);
-        const int L = __ffs(sel) - 1;
-        const uint32_t base_cnt = __shfl_sync(0xffffffffu, exc, L);
-        // inside lane L's slice: per words, each lane takes per/32 words
-        uint32_t bucket = 0, below = 0;
-        {
-          const int wpl = per >> 5 > 0 ? per >> 5 : 1;  // words per lane in the slice
-          const int w0 = L * per + lane * wpl;
-          uint32_t cnt = 0;
-          if (lane * wpl < per)
-            for (int j = 0; j < wpl; ++j) {
-              const uint32_t q = hist[w0 + j];
-              cnt += (q & 0xffffu) + (q >> 16);
-            }
-          uint32_t inc2 = cnt;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t t = __shfl_up_sync(0xffffffffu, inc2, o);
-            if (lane >= o) inc2 += t;
-          }
-          const uint32_t exc2 = base_cnt + inc2 - cnt;
-          const bool here = lane * wpl < per && exc2 <= (uint32_t)r && (uint32_t)r < exc2 + cnt;
-          const uint32_t sel2 = __ballot_sync(0xffffffffu, here);
-          const int L2 = __ffs(sel2) - 1;
-          if (lane == L2) {
-            uint32_t acc = exc2;
-            for (int j = 0; j < wpl; ++j) {
-              const uint32_t q = hist[w0 + j];
-              const uint32_t c0 = q & 0xffffu, c1 = q >> 16;
-              const uint32_t word = (uint32_t)(w0 + j);
-              if ((uint32_t)r < acc + c0) { bucket = word * 2; below = acc; break; }
-              acc += c0;
-              if ((uint32_t)r < acc + c1) { bucket = word * 2 + 1; below = acc; break; }
-              acc += c1;
-            }
-          }
-          bucket = __shfl_sync(0xffffffffu, bucket, L2);
-          below = __shfl_sync(0xffffffffu, below, L2);
-        }
-        r -= (int)below;
-        prefix |= (K)bucket << sh;
-        pmask |= (K)dmask << sh;
-        __syncwarp();
-      }
-      // r-th occurrence (index order) of key == prefix.  Fully unrolled so the
-      // key array stays in registers.
-      int cnt[NI];
-      int fi = -1;
-#pragma unroll
-      for (int i = 0; i < NI; ++i) {
-        int c_i = 0;
+      for (int i = 0; i < NI; ++i)
 #pragma unroll
         for (int c = 0; c < VW; ++c) {
-          const int pos = i * 32 * VW + lane * VW + c;
-          c_i += (pos < N && key[i][c] == prefix) ? 1 : 0;
+          const int e = ((i * RG + w) * 32 + lane) * VW + c;
+          if (e < N && Tr::isnan_(xr[e]) && (unsigned long long)e < mine) mine = e;
         }
-        cnt[i] = c_i;
-        const int total = (int)__reduce_add_sync(0xffffffffu, (unsigned)c_i);
-        if (fi < 0) {
-          if (r < total) fi = i;
-          else r -= total;
+      if (RG == 1) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, mine, o);
+          mine = other < mine ? other : mine;
+        }
+        if (lane == 0) S.first_nan = mine;
+      } else if (mine != ~0ull) {
+        atomicMin(&S.first_nan, mine);
+      }
+      group_sync<RG>(g);
+      if (t == 0) {
+        idxs[row] = (int64_t)S.first_nan;
+        vals[row] = xr[S.first_nan];
+      }
+      group_sync<RG>(g);
+      continue;
+    }
+
+    // ---- pass 0 over registers: top DIG0 bits
+#pragma unroll
+    for (int i = 0; i < NI; ++i)
+#pragma unroll
+      for (int c = 0; c < VW; ++c) {
+        const int e = ((i * RG + w) * 32 + lane) * VW + c;
+        if (e < N) hist_add(S.hist, key[i][c] >> SH0);
+      }
+    group_sync<RG>(g);
+    uint32_t b0, below, cnt;
+    group_find<RG>(S, g, 1 << DIG0, (uint32_t)k, b0, below, cnt);
+    uint32_t r = (uint32_t)k - below;
+
+    // ---- compact the bucket's elements as (key << 32 | index)
+#pragma unroll
+    for (int i = 0; i < NI; ++i)
+#pragma unroll
+      for (int c = 0; c < VW; ++c) {
+        const int e = ((i * RG + w) * 32 + lane) * VW + c;
+        if (e < N && (key[i][c] >> SH0) == b0) {
+          const uint32_t pos = atomicAdd(&S.ncand, 1u);
+          S.list[pos] = ((unsigned long long)key[i][c] << 32) | (uint32_t)e;
         }
       }
-      int my = 0;
+    group_sync<RG>(g);
+    const uint32_t C = cnt;  // == S.ncand
+    unsigned long long ans = 0;
+    if (C <= 32) {
+      // one warp: bitonic sort of <= 32 composites, pick the r-th
+      if (w == 0) {
+        unsigned long long v = lane < (int)C ? S.list[lane] : ~0ull;
 #pragma unroll
-      for (int i = 0; i < NI; ++i) my = (i == fi) ? cnt[i] : my;
-      int inc = my;
+        for (int kk = 2; kk <= 32; kk <<= 1) {
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += t;
-      }
-      const int exc = inc - my;
-      const uint32_t sel = __ballot_sync(0xffffffffu, fi >= 0 && exc <= r && r < inc);
-      found_lane = sel ? __ffs(sel) - 1 : 0;
-      int cc = 0, rr = r - exc;
-#pragma unroll
-      for (int i = 0; i < NI; ++i) {
-        if (i == fi) {
-#pragma unroll
-          for (int c = 0; c < VW; ++c) {
-            const int pos = i * 32 * VW + lane * VW + c;
-            if (pos < N && key[i][c] == prefix) {
-              if (rr == 0) cc = c;
-              --rr;
-            }
+          for (int j = kk >> 1; j > 0; j >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, j);
+            const bool up = ((lane & kk) == 0);
+            const bool lower = ((lane & j) == 0);
+            const unsigned long long mn = o < v ? o : v, mx = o < v ? v : o;
+            v = (lower == up) ? mn : mx;
           }
         }
+        ans = __shfl_sync(0xffffffffu, v, r);
+        if (lane == 0) S.list[0] = ans;  // publish (list no longer needed)
       }
-      found_c = __shfl_sync(0xffffffffu, cc, found_lane);
-      found_i = fi;
+      group_sync<RG>(g);
+      ans = S.list[0];
+    } else {
+      // radix passes over the list: remaining key bits, then the index bits
+      // composite digit source: c = (key << 32) | idx; key bits [SH0-1 .. 0], idx bits [10..0]
+      unsigned long long pref = 0, pmask = 0;
+      const int nb_key = SH0;  // remaining key bits
+      // pass plan over a virtual (nb_key + 11)-bit value v = (key & lowmask) << 11 | idx
+      const int tot_bits = nb_key + 11;
+      for (int done = 0; done < tot_bits;) {
+        const int wbits = (tot_bits - done) < DIGL ? (tot_bits - done) : DIGL;
+        const int sh = tot_bits - done - wbits;
+        group_sync<RG>(g);
+        group_clear_hist<RG>(S, 1 << DIGL);
+        group_sync<RG>(g);
+        for (uint32_t q = t; q < C; q += RG * 32) {
+          const unsigned long long cpx = S.list[q];
+          const unsigned long long vv =
+              ((cpx >> 32) & ((1ull << nb_key) - 1ull)) << 11 | (cpx & 0x7ffull);
+          if ((vv & pmask) == pref) hist_add(S.hist, (uint32_t)(vv >> sh) & ((1u << wbits) - 1u));
+        }
+        group_sync<RG>(g);
+        uint32_t bb, bl, bc;
+        group_find<RG>(S, g, 1 << DIGL, r, bb, bl, bc);
+        r -= bl;
+        pref |= (unsigned long long)bb << sh;
+        pmask |= (unsigned long long)((1u << wbits) - 1u) << sh;
+        done += wbits;
+      }
+      // pref now holds (remaining key bits, index)
+      ans = ((unsigned long long)b0 << (32 + SH0)) | ((pref >> 11) << 32) | (pref & 0x7ffull);
     }
-    if (lane == 0) {
-      int64_t pos = (int64_t)found_i * 32 * VW + found_lane * VW + found_c;
-      if (found_i < 0 || pos >= N) pos = 0;  // unreachable; keeps the read in bounds
-      idxs[row] = pos;
-      vals[row] = xr[pos];
+    if (t == 0) {
+      int64_t e = (int64_t)(uint32_t)ans;
+      if (e >= N) e = 0;  // unreachable; keeps the read in bounds
+      idxs[row] = e;
+      vals[row] = xr[e];
     }
+    group_sync<RG>(g);
   }
 }
 
@@ -415,31 +459,42 @@ median_cta_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __rest
 // ---------------------------------------------------------------------------
 // dispatch
 // ---------------------------------------------------------------------------
-template <typename T, int NI, int VW>
-int launch_warp(const void* x, void* v, int64_t* idx, int64_t M, int N, cudaStream_t st) {
-  constexpr int WARPS = 8;
+template <typename T, int RG, int NI, int VW, int DIG0>
+int launch_group(const void* x, void* v, int64_t* idx, int64_t M, int N, cudaStream_t st) {
+  constexpr int GPC = 8 / RG;                 // groups per CTA (256 threads)
+  constexpr int DIGL = RG == 1 ? 8 : 11;      // digit width of the list passes
+  auto kern = median_group_kernel<T, RG, NI, VW, DIG0, DIGL, GPC>;
+  const int smem = (int)(GPC * sizeof(GroupSmemOf<RG, NI, VW, DIG0, DIGL>));
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+    set_error("median: cannot reserve %d bytes of shared memory", smem);
+    return FO_ECUDA;
+  }
   int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, median_warp_kernel<T, NI, VW, WARPS>,
-                                                WARPS * 32, 0);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GPC * RG * 32, smem);
   if (per_sm < 1) per_sm = 1;
-  int64_t need = (M + WARPS - 1) / WARPS;
+  const int64_t need = (M + GPC - 1) / GPC;
   int64_t grid = (int64_t)num_sms() * per_sm;
   if (grid > need) grid = need;
-  median_warp_kernel<T, NI, VW, WARPS><<<(unsigned)grid, WARPS * 32, 0, st>>>(
-      (const T*)x, (T*)v, idx, M, N);
-  return check_launch("median_warp_kernel");
+  kern<<<(unsigned)grid, GPC * RG * 32, smem, st>>>((const T*)x, (T*)v, idx, M, N);
+  return check_launch("median_group_kernel");
 }
 
-template <typename T, int VW>
-int pick_ni(const void* x, void* v, int64_t* idx, int64_t M, int N, cudaStream_t st) {
-  const int ni = (N + 32 * VW - 1) / (32 * VW);
-  if (ni <= 1) return launch_warp<T, 1, VW>(x, v, idx, M, N, st);
-  if (ni <= 2) return launch_warp<T, 2, VW>(x, v, idx, M, N, st);
-  if (ni <= 4) return launch_warp<T, 4, VW>(x, v, idx, M, N, st);
-  if (ni <= 8) return launch_warp<T, 8, VW>(x, v, idx, M, N, st);
-  if (ni <= 16) return launch_warp<T, 16, VW>(x, v, idx, M, N, st);
-  if (VW == 1 && ni <= 32) return launch_warp<T, 32, 1>(x, v, idx, M, N, st);
-  return launch_warp<T, 64, 1>(x, v, idx, M, N, st);
+// Row length -> group width RG (warps), slots NI per lane, vector width VW.
+template <typename T>
+int dispatch_group(const void* x, void* v, int64_t* idx, int64_t M, int N, bool vec,
+                   cudaStream_t st) {
+  constexpr int VWV = 16 / sizeof(T);
+  if (vec) {
+    // 16-byte vectors: 32 * RG * NI * VWV >= N
+    if (N <= 32 * VWV * 4) return launch_group<T, 1, 4, VWV, 8>(x, v, idx, M, N, st);
+    if (N <= 64 * VWV * 4) return launch_group<T, 2, 4, VWV, 11>(x, v, idx, M, N, st);
+    return launch_group<T, 4, 4, VWV, 11>(x, v, idx, M, N, st);
+  }
+  if (N <= 256) return launch_group<T, 1, 8, 1, 8>(x, v, idx, M, N, st);
+  if (N <= 512) return launch_group<T, 1, 16, 1, 8>(x, v, idx, M, N, st);
+  if (N <= 1024) return launch_group<T, 2, 16, 1, 11>(x, v, idx, M, N, st);
+  return launch_group<T, 4, 16, 1, 11>(x, v, idx, M, N, st);
 }
 
 template <typename T>
@@ -454,9 +509,8 @@ template <typename T>
 int median_dim_t(const void* x, void* v, int64_t* idx, int64_t M, int64_t N, cudaStream_t st) {
   if (sizeof(T) <= 4 && N <= 2048) {
     constexpr int VWV = 16 / (sizeof(T) <= 4 ? sizeof(T) : 4);
-    const bool vec = aligned16(x) && ((N * (int64_t)sizeof(T)) % 16 == 0);
-    if (vec && N >= 32 * VWV) return pick_ni<T, VWV>(x, v, idx, M, (int)N, st);
-    return pick_ni<T, 1>(x, v, idx, M, (int)N, st);
+    const bool vec = aligned16(x) && ((N * (int64_t)sizeof(T)) % 16 == 0) && N >= 32 * VWV;
+    return dispatch_group<T>(x, v, idx, M, (int)N, vec, st);
   }
   return launch_cta<T>(x, v, idx, M, N, st);
 }
