@@ -531,3 +531,82 @@ extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, 
   return dispatch_dtype<int32_t>(dtype, reduce, out, src, index, g, og, n, include_self != 0, pl,
                                  workspace, err_count, st);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot allocate device memory at the moment they need a
+// scatter: a host framework that owns the whole device heap (pre-reserved
+// memory pools that forbid any other allocation), a foreign-function caller
+// (cgo, JNI, a plugin host) that has no handle to the program's allocator, or
+// code that must not pay the implicit device synchronisation a cudaMalloc can
+// trigger.  For them the scratch (accumulator + counts) lives in one
+// file-scope device array, reserved when the library is loaded on a device and
+// held by every device that loads it until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace fo {
+namespace {
+// Accumulator + counts for up to 2^20 output cells (8-byte accumulators
+// included): 12 MiB per device.
+constexpr size_t kNoAllocScratchBytes = (size_t)12 << 20;
+__device__ __align__(256) unsigned char g_scatter_scratch[kNoAllocScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {nullptr};
+
+// Device address of g_scatter_scratch on the current device (looked up once per
+// device; the symbol's name in host code is not a device address).
+int scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("scatter_reduce_noalloc: no usable current device");
+    return FO_ECUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_scatter_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("scatter_reduce_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return FO_ECUDA;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return FO_OK;
+}
+}  // namespace
+}  // namespace fo
+
+extern "C" int fo_scatter_reduce_noalloc(void* out, const void* src, const void* index, int ndim,
+                                         const int64_t* index_shape,
+                                         const int64_t* index_strides,
+                                         const int64_t* src_strides, const int64_t* out_shape,
+                                         const int64_t* out_strides, int dim, int reduce,
+                                         int include_self, int dtype, int index_dtype,
+                                         int32_t* err_count, void* stream) {
+  clear_error();
+  FO_CHECK_ARG(ndim >= 1 && ndim <= 4, "scatter_reduce supports 1-4-D tensors, got %dD", ndim);
+  FO_CHECK_ARG(out_shape && out_strides, "scatter_reduce_noalloc: null shape/stride array");
+  FO_CHECK_ARG(reduce >= FO_SUM && reduce <= FO_AMIN, "Unsupported reduce code %d", reduce);
+  const int64_t span = out_span(out_shape, out_strides, ndim);
+  const Plan pl = make_plan(reduce, include_self != 0, dtype, span);
+  const size_t need = pl.acc_bytes + pl.cnt_bytes;
+  if (need > kNoAllocScratchBytes) {
+    set_error("scatter_reduce_noalloc: this call needs %zu bytes of scratch but the static "
+              "scratch holds %zu (at most 2^20 output cells); use fo_scatter_reduce with a "
+              "caller-provided workspace", need, kNoAllocScratchBytes);
+    return FO_EWORKSPACE;
+  }
+  void* ws = nullptr;
+  if (need > 0) {
+    if (int rc = scratch_address(&ws)) return rc;
+  }
+  // The scratch keeps the previous call's contents; the init pass of the
+  // scatter clears every byte this call reads before it is used.
+  return fo_scatter_reduce(out, src, index, ndim, index_shape, index_strides, src_strides,
+                           out_shape, out_strides, dim, reduce, include_self, dtype, index_dtype,
+                           ws, (int64_t)kNoAllocScratchBytes, err_count, stream);
+}

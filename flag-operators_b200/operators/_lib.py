@@ -44,6 +44,9 @@ _SIGS = {
     "fo_scatter_reduce": [_c_void_p, _c_void_p, _c_void_p, _int, _i64p, _i64p, _i64p, _i64p,
                           _i64p, _int, _int, _int, _int, _int, _c_void_p, _i64, _c_void_p,
                           _c_void_p],
+    "fo_scatter_reduce_noalloc": [_c_void_p, _c_void_p, _c_void_p, _int, _i64p, _i64p, _i64p,
+                                  _i64p, _i64p, _int, _int, _int, _int, _int, _c_void_p,
+                                  _c_void_p],
     "fo_ce_workspace_bytes": [_i64, _i64p],
     "fo_ce_fwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                   _i64, _i64, _i64, _i64, _f32, _int, _int, _c_void_p, _i64, _c_void_p],

@@ -127,6 +127,27 @@ FO_API int fo_scatter_reduce(void* out, const void* src, const void* index, int 
                       void* workspace, int64_t ws_bytes, int32_t* err_count,
                       void* stream);
 
+/*
+ * Allocation-free scatter_reduce: same arguments and results as
+ * fo_scatter_reduce, without the workspace.  No counterpart in the reference.
+ * For callers that cannot allocate device memory (a framework that owns the
+ * whole device heap, a cgo / JNI / plugin caller without the program's
+ * allocator, code that must avoid the device synchronisation of cudaMalloc).
+ * The scratch is one static 12 MiB device array per device, reserved when the
+ * library is loaded and held until the process exits; it covers up to 2^20
+ * output cells and larger calls fail with FO_EWORKSPACE.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress), so make
+ * that first call before any stream capture.  Every call reuses the same array
+ * (it is re-initialised per call): calls that overlap on the GPU, from several
+ * streams or threads, race and must not be issued.  Allocates nothing.
+ */
+FO_API int fo_scatter_reduce_noalloc(void* out, const void* src, const void* index, int ndim,
+                                     const int64_t* index_shape, const int64_t* index_strides,
+                                     const int64_t* src_strides, const int64_t* out_shape,
+                                     const int64_t* out_strides, int dim, int reduce,
+                                     int include_self, int dtype, int index_dtype,
+                                     int32_t* err_count, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* fused cross-entropy                                                       */
 /* ------------------------------------------------------------------------ */
