@@ -53,25 +53,30 @@ constexpr int kD = 128;
 constexpr int kThr = 256;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
-// shared-memory map (bytes from a 1024-aligned base)
-constexpr uint32_t OFF_QK = 0;         // 2 x [128 x 128B]: rows 0-63 Q (later gQ), 64-127 K (later gK)
-constexpr uint32_t OFF_V = 32768;      // 2 x [64 x 128B]
-constexpr uint32_t OFF_KT = 49152;     // 2 x [64 x 128B]  Kt
-constexpr uint32_t OFF_T = 65536;      // [64 x 128B]      T
-constexpr uint32_t OFF_P = 73728;      // [64 x 128B]      P
-constexpr uint32_t OFF_WT = 81920;     // [128 x 128B]     -W^T
-constexpr uint32_t OFF_S = 98304;      // 2 x [128 x 128B] state (fp16 copy)
-constexpr uint32_t OFF_UT = 131072;    // [128 x 128B]     U^T; then output staging [64 x 256B]
-constexpr uint32_t OFF_RAW = 147456;   // [3][64 x 256B]   next chunk's q, k, v rows (bulk copy)
-constexpr uint32_t OFF_A = 196608;     // fp32 [64][68]    A (rows 16-byte aligned)
-constexpr uint32_t OFF_G = 214016;     // gate tables + barriers
+// shared-memory map (bytes from a 1024-aligned base).  Owner: P = prep warps,
+// C = chain warps, P->C = written by prep, read by the chain (single buffer,
+// guarded by the chain's MMA-completion barriers).
+constexpr uint32_t OFF_QK = 0;         // P    2 x [128 x 128B]: rows 0-63 Q, 64-127 K (then gK)
+constexpr uint32_t OFF_V = 32768;      // P    2 x [64 x 128B]   V
+constexpr uint32_t OFF_GQ = 49152;     // P->C 2 x [64 x 128B]   gQ
+constexpr uint32_t OFF_KT = 65536;     // P->C 2 x [64 x 128B]   Kt
+constexpr uint32_t OFF_WT = 81920;     // P->C [128 x 128B]      -W^T (T [64 x 128B] before it)
+constexpr uint32_t OFF_P = 98304;      // C    [64 x 128B]       P
+constexpr uint32_t OFF_S = 106496;     // C    2 x [128 x 128B]  state (fp16 copy)
+constexpr uint32_t OFF_UT = 139264;    // C    [128 x 128B]      U^T; then output staging [64 x 256B]
+constexpr uint32_t OFF_RAW = 155648;   // P    [3][64 x 256B]    q, k, v rows of the next chunk
+constexpr uint32_t OFF_A = 204800;     // P    fp32 [64][68]     A (rows 16-byte aligned)
+constexpr uint32_t OFF_G = 222208;     // gate tables x 2 (P->C), then barriers
 constexpr int kAStride = 68;
+constexpr uint32_t kGateBytes = 2304;
 constexpr uint32_t G_LC = 0, G_Z = 256, G_NEG = 512, G_BETA = 768, G_GAM = 1024, G_GAMP = 1280,
-                   G_KTS = 1536, G_MISC = 1792;
-constexpr uint32_t kSmemBytes = OFF_G + 2048 + 1024;  // + alignment slack
+                   G_KTS = 1536, G_SB = 1792, G_GC = 2048;
+constexpr uint32_t OFF_BAR = OFF_G + 2 * kGateBytes;
+constexpr uint32_t kSmemBytes = OFF_BAR + 128 + 1024;  // + alignment slack
 
-// TMEM columns (fp32 accumulators, 128 lanes)
-constexpr uint32_t TM_S = 0, TM_U = 128, TM_O = 192, TM_QK = 256, TM_W = 320, TM_COLS = 512;
+// TMEM columns (fp32 accumulators, 128 lanes): chain-owned S, O; double-buffered
+// U (prep writes U0, chain accumulates and reads) and QK^T/KK^T; prep-owned W.
+constexpr uint32_t TM_S = 0, TM_O = 128, TM_U0 = 192, TM_QK0 = 320, TM_W = 448, TM_COLS = 512;
 
 // element type of every tensor-core operand tile
 using Op = __half;
@@ -109,6 +114,14 @@ __device__ __forceinline__ uint4 scale8(uint4 u, float s) {
   return r;
 }
 
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// lc: in-chunk prefix sums of log2|g|; z: last zero-gate index (-1 if none);
+// neg: prefix count of negative gates.
 struct GateTabs {
   const float* lc;
   const int* z;
@@ -119,7 +132,7 @@ struct GateTabs {
     if (z[t] > s) return 0.f;
     const float e = lc[t] - (s >= 0 ? lc[s] : 0.f);
     const int par = (neg[t] - (s >= 0 ? neg[s] : 0)) & 1;
-    const float r = expf(e);
+    const float r = exp2f(e);
     return par ? -r : r;
   }
 };
@@ -139,22 +152,22 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~(uintptr_t)1023);
   const uint32_t sb = tc::smem_u32(sm);
-  float* sLc = reinterpret_cast<float*>(sm + OFF_G + G_LC);
-  int* sZ = reinterpret_cast<int*>(sm + OFF_G + G_Z);
-  int* sNeg = reinterpret_cast<int*>(sm + OFF_G + G_NEG);
-  float* sBeta = reinterpret_cast<float*>(sm + OFF_G + G_BETA);
-  float* sGam = reinterpret_cast<float*>(sm + OFF_G + G_GAM);
-  float* sGamP = reinterpret_cast<float*>(sm + OFF_G + G_GAMP);
-  float* sKts = reinterpret_cast<float*>(sm + OFF_G + G_KTS);
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + OFF_G + G_MISC);
-  uint64_t* rawbar = reinterpret_cast<uint64_t*>(sm + OFF_G + G_MISC + 8);
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_G + G_MISC + 16);
-  int* s_abort = reinterpret_cast<int*>(sm + OFF_G + G_MISC + 20);
-  float* s_gc = reinterpret_cast<float*>(sm + OFF_G + G_MISC + 24);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* bar_raw = bars + 0;    // bulk copy of a chunk landed            (prep)
+  uint64_t* bar_pmma = bars + 1;   // prep's MMAs completed                  (prep)
+  uint64_t* bar_prep = bars + 2;   // prep products of a chunk ready         (prep -> chain)
+  uint64_t* bar_b1 = bars + 3;     // chain MMAs (d),(e) completed           (chain -> both)
+  uint64_t* bar_b2 = bars + 4;     // chain MMAs (f),(g) completed           (chain -> both)
+  uint64_t* bar_done = bars + 5;   // [2] chain finished a chunk (per buffer) (chain -> prep)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 64);
+  int* s_abort = reinterpret_cast<int*>(sm + OFF_BAR + 68);
   float* sA = reinterpret_cast<float*>(sm + OFF_A);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int quad = warp & 3, colh = warp >> 2;
+  const bool is_chain = warp < 4;
+  const int gt_id = is_chain ? tid : tid - 128;   // thread index inside its group
+  const int quad = warp & 3;                      // TMEM lane quadrant
+  const int row = 32 * quad + lane;               // TMEM lane = accumulator row
   const int64_t head = blockIdx.x;
   const T* qh = q + head * L * kD;
   const T* kh = k + head * L * kD;
@@ -163,16 +176,15 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   const G* bh = beta + head * L;
   const G* gh = g + head * L;
   constexpr bool BF = false;  // operands are fp16
-  const GateTabs gt{sLc, sZ, sNeg};
   const int64_t nchunks = (L + kC - 1) / kC;
+  const int bar_id = is_chain ? 1 : 2;            // named barrier of the group
 
   if (warp == 0) {
     tc::tmem_alloc(s_tmem, TM_COLS);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    tc::mbar_init(mbar, 1);
-    tc::mbar_init(rawbar, 1);
+    for (int b = 0; b < 7; ++b) tc::mbar_init(bars + b, 1);
     tc::fence_mbar_init();
     *s_abort = 0;
   }
@@ -181,335 +193,366 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   tc::fence_after_sync();
   const uint32_t tm = *s_tmem;
   const uint32_t tm_lane = tm + ((uint32_t)(32 * quad) << 16);
-  uint32_t phase = 0, rphase = 0;
-  bool state_nz = false;
 
-  // q, k, v rows of chunk c -> RAW (bulk copies, completion on rawbar)
-  auto issue_raw = [&](int64_t c) {
-    const int64_t t0 = c * kC;
-    const int nv = (int)((L - t0) < kC ? (L - t0) : kC);
-    const uint32_t bytes = (uint32_t)nv * kD * sizeof(T);
-    tc::mbar_arrive_expect_tx(rawbar, 3 * bytes);
-    tc::bulk_g2s(sm + OFF_RAW, qh + t0 * kD, bytes, rawbar);
-    tc::bulk_g2s(sm + OFF_RAW + 16384, kh + t0 * kD, bytes, rawbar);
-    tc::bulk_g2s(sm + OFF_RAW + 32768, vh + t0 * kD, bytes, rawbar);
+  auto gsync = [&]() {
+    tc::fence_before_sync();
+    asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+    tc::fence_after_sync();
   };
-  // thread 0 polls an mbarrier (bounded); the CTA barrier publishes the outcome
-  auto bar_wait = [&](uint64_t* bar, uint32_t& ph) {
-    if (tid == 0) {
-      if (!tc::mbar_wait(bar, ph, kWaitLimit)) {
+  // One elected thread of the group polls the mbarrier (bounded); a reducing
+  // group barrier hands every thread of the group the same abort decision, so a
+  // timeout (or the other group giving up) can never split a group across a
+  // barrier.  Returns true when the group must stop.
+  auto gwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    int bad = 0;
+    if (gt_id == 0) {
+      if (*reinterpret_cast<volatile int*>(s_abort)) {
+        bad = 1;
+      } else if (!tc::mbar_wait(bar, parity, kWaitLimit)) {
         atomicAdd(&g_gdr_timeouts, 1u);
-        *s_abort = 1;
+        *reinterpret_cast<volatile int*>(s_abort) = 1;
+        bad = 1;
       }
     }
-    ph ^= 1u;
-    cta_sync_tc();
+    tc::fence_before_sync();
+    int any;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, 128, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(any)
+        : "r"(bad), "r"(bar_id)
+        : "memory");
+    tc::fence_after_sync();
+    return any != 0;
   };
-  auto mma_wait = [&]() { bar_wait(mbar, phase); };
+  auto gtab = [&](int b) { return sm + OFF_G + b * kGateBytes; };
 
-  if (tid == 0 && nchunks > 0) issue_raw(0);
-
-  // ---- initial state
-  if (h0) {
-    const float* hh = h0 + head * kD * kD;
-    const int i = 32 * quad + lane;  // state row (value channel)
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int j0 = 64 * colh + 32 * half;
-      uint32_t r[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(hh[i * kD + j0 + j]);
-      tc::tmem_st32(tm_lane + TM_S + j0, r);
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint4 pk;
-        pk.x = pack2<Op>(__uint_as_float(r[8 * c4 + 0]), __uint_as_float(r[8 * c4 + 1]));
-        pk.y = pack2<Op>(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
-        pk.z = pack2<Op>(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
-        pk.w = pack2<Op>(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
-        *reinterpret_cast<uint4*>(sm + OFF_S + colh * 16384 + tc::sw128_chunk(i, 4 * half + c4)) =
-            pk;
-      }
+  if (!is_chain) {
+    // =====================================================================
+    // prep warps: everything of a chunk that does not need the state
+    // =====================================================================
+    const int p = gt_id;
+    uint32_t raw_phase = 0, pmma_phase = 0;
+    auto issue_raw = [&](int64_t c) {
+      const int64_t t0 = c * kC;
+      const int nv = (int)((L - t0) < kC ? (L - t0) : kC);
+      const uint32_t bytes = (uint32_t)nv * kD * sizeof(T);
+      tc::mbar_arrive_expect_tx(bar_raw, 3 * bytes);
+      tc::bulk_g2s(sm + OFF_RAW, qh + t0 * kD, bytes, bar_raw);
+      tc::bulk_g2s(sm + OFF_RAW + 16384, kh + t0 * kD, bytes, bar_raw);
+      tc::bulk_g2s(sm + OFF_RAW + 32768, vh + t0 * kD, bytes, bar_raw);
+    };
+    auto pmma_wait = [&]() -> bool {
+      const bool bad = gwait(bar_pmma, pmma_phase);
+      pmma_phase ^= 1u;
+      return bad;
+    };
+    if (p == 0 && nchunks > 0) issue_raw(0);
+    float nb_gate = 0.f, ng_gate = 1.f;
+    if (p < 64 && p < L) {
+      nb_gate = to_f<G>(bh[p]);
+      ng_gate = to_f<G>(gh[p]);
     }
-    tc::tmem_wait_st();
-    state_nz = true;
-  }
-
-  for (int64_t c = 0; c < nchunks; ++c) {
-    const int64_t tok0 = c * kC;
-    const int nvalid = (int)((L - tok0) < kC ? (L - tok0) : kC);
-
-    // ---- gates (small direct loads) while the bulk copy lands
-    if (tid < 64) {
-      const bool ok = tid < nvalid;
-      const float bt = ok ? to_f<G>(bh[tok0 + tid]) : 0.f;
-      const float gg = ok ? to_f<G>(gh[tok0 + tid]) : 1.f;
-      sBeta[tid] = bt;
-      // prefix sums over the chunk: log|g|, last zero-gate index, negative count
-      float lg = (gg != 0.f) ? logf(fabsf(gg)) : 0.f;
-      int zi = (gg == 0.f) ? tid : -1;
-      int ng = (gg < 0.f) ? 1 : 0;
+    for (int64_t c = 0; c < nchunks; ++c) {
+      const int b = (int)(c & 1);
+      const int64_t tok0 = c * kC;
+      const int nvalid = (int)((L - tok0) < kC ? (L - tok0) : kC);
+      uint8_t* G0 = gtab(b);
+      float* sLc = reinterpret_cast<float*>(G0 + G_LC);
+      int* sZ = reinterpret_cast<int*>(G0 + G_Z);
+      int* sNeg = reinterpret_cast<int*>(G0 + G_NEG);
+      float* sBeta = reinterpret_cast<float*>(G0 + G_BETA);
+      const GateTabs gt{sLc, sZ, sNeg};
+      // buffers QK[b], U[b] and gate table b were last used by chunk c - 2
+      if (c >= 2 && gwait(bar_done + b, (uint32_t)(((c - 2) >> 1) & 1))) break;
+      if (p < 64) {
+        const float bt = nb_gate, gg = ng_gate;
+        const int64_t t1 = tok0 + kC + p;
+        nb_gate = t1 < L ? to_f<G>(bh[t1]) : 0.f;
+        ng_gate = t1 < L ? to_f<G>(gh[t1]) : 1.f;
+        sBeta[p] = bt;
+        float lg = (gg != 0.f) ? log2f(fabsf(gg)) : 0.f;
+        int zi = (gg == 0.f) ? p : -1;
+        int ng = (gg < 0.f) ? 1 : 0;
 #pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float a = __shfl_up_sync(0xffffffffu, lg, off);
-        const int bz = __shfl_up_sync(0xffffffffu, zi, off);
-        const int bn = __shfl_up_sync(0xffffffffu, ng, off);
-        if (lane >= off) {
-          lg += a;
-          zi = max(zi, bz);
-          ng += bn;
+        for (int off = 1; off < 32; off <<= 1) {
+          const float a = __shfl_up_sync(0xffffffffu, lg, off);
+          const int bz = __shfl_up_sync(0xffffffffu, zi, off);
+          const int bn = __shfl_up_sync(0xffffffffu, ng, off);
+          if (lane >= off) {
+            lg += a;
+            zi = max(zi, bz);
+            ng += bn;
+          }
         }
+        sLc[p] = lg;
+        sZ[p] = zi;
+        sNeg[p] = ng;
       }
-      sLc[tid] = lg;
-      sZ[tid] = zi;
-      sNeg[tid] = ng;
-    }
-    bar_wait(rawbar, rphase);  // includes a CTA barrier
-    if (*s_abort) break;
-    if (tid >= 32 && tid < 64) {
-      sLc[tid] += sLc[31];
-      sZ[tid] = max(sZ[tid], sZ[31]);
-      sNeg[tid] += sNeg[31];
-    }
-    // RAW (T, row-major) -> fp16 swizzled operand tiles; rows past the end are zero
-    for (int idx = tid; idx < 3 * 1024; idx += kThr) {
-      const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
-      const int half = ch >> 3, cc = ch & 7;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (t < nvalid)
-        val = to_op8<T>(*reinterpret_cast<const uint4*>(sm + OFF_RAW + m * 16384 + t * 256 + ch * 16));
-      uint32_t off;
-      if (m == 0) off = OFF_QK + half * 16384 + tc::sw128_chunk(t, cc);
-      else if (m == 1) off = OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc);
-      else off = OFF_V + half * 8192 + tc::sw128_chunk(t, cc);
-      *reinterpret_cast<uint4*>(sm + off) = val;
-    }
-    __syncthreads();
-    if (tid == 0 && c + 1 < nchunks) {
-      tc::fence_proxy_async();  // RAW was read through the generic proxy
-      issue_raw(c + 1);
-    }
-    if (tid < 64) {
-      sGam[tid] = gt.ratio(tid, -1);
-      sGamP[tid] = tid > 0 ? gt.ratio(tid - 1, -1) : 1.f;
-      sKts[tid] = gt.ratio(kC - 1, tid) * sBeta[tid];
-      if (tid == 0) *s_gc = gt.ratio(kC - 1, -1);
-    }
-    tc::fence_proxy_async();
-    cta_sync_tc();
-
-    // ---- (a) [Q;K] K^T -> TM_QK
-    if (tid == 0) {
-      constexpr uint32_t id_a = tc::idesc_f16(128, 64, BF, false, false);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t h = ks >> 2, kk = ks & 3;
-        const uint64_t da = tc::desc_sw128(sb + OFF_QK + h * 16384 + kk * 32, 16, 1024);
-        const uint64_t db = tc::desc_sw128(sb + OFF_QK + h * 16384 + 8192 + kk * 32, 16, 1024);
-        tc::mma_f16(tm + TM_QK, da, db, id_a, ks > 0);
+      const bool raw_bad = gwait(bar_raw, raw_phase);
+      raw_phase ^= 1u;
+      if (raw_bad) break;
+      if (p >= 32 && p < 64) {
+        sLc[p] += sLc[31];
+        sZ[p] = max(sZ[p], sZ[31]);
+        sNeg[p] += sNeg[31];
       }
-      tc::mma_commit(mbar);
-    }
-    mma_wait();
-    if (*s_abort) break;
-
-    // ---- P (rows 0-63) and A (rows 64-127) from the QK / KK block
-    {
-      uint32_t r[32];
-      tc::tmem_ld32(tm_lane + TM_QK + 32 * colh, r);
-      tc::tmem_wait_ld();
-      const int row = 32 * quad + lane;
-      if (row < 64) {
-        const int t = row;
-        float pv[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int s = 32 * colh + j;
-          pv[j] = (s <= t) ? gt.ratio(t, s) * sBeta[s] * __uint_as_float(r[j]) : 0.f;
-        }
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint4 pk;
-          pk.x = pack2<Op>(pv[8 * c4 + 0], pv[8 * c4 + 1]);
-          pk.y = pack2<Op>(pv[8 * c4 + 2], pv[8 * c4 + 3]);
-          pk.z = pack2<Op>(pv[8 * c4 + 4], pv[8 * c4 + 5]);
-          pk.w = pack2<Op>(pv[8 * c4 + 6], pv[8 * c4 + 7]);
-          *reinterpret_cast<uint4*>(sm + OFF_P + tc::sw128_chunk(t, 4 * colh + c4)) = pk;
-        }
-      } else {
-        const int t = row - 64;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int s = 32 * colh + j;
-          sA[t * kAStride + s] =
-              (s < t) ? gt.ratio(t - 1, s) * sBeta[s] * __uint_as_float(r[j]) : 0.f;
-        }
-      }
-    }
-    cta_sync_tc();
-
-    if (tid < 64) {
-      // ---- T = (I + A)^-1 by forward substitution, one column per thread:
-      //      T[i][j] = [i == j] - sum_{m < i} A[i][m] T[m][j]
-      // The column lives in registers; row i of A is a broadcast read.
-      const int j = tid;
-      float col[kC];
-#pragma unroll
-      for (int i = 0; i < kC; ++i) {
-        float acc0 = (i == j) ? 1.f : 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-#pragma unroll
-        for (int m = 0; m < i; m += 4) {
-          const float4 a4 = *reinterpret_cast<const float4*>(sA + i * kAStride + m);
-          acc0 = fmaf(-a4.x, col[m], acc0);
-          if (m + 1 < i) acc1 = fmaf(-a4.y, col[m + 1], acc1);
-          if (m + 2 < i) acc2 = fmaf(-a4.z, col[m + 2], acc2);
-          if (m + 3 < i) acc3 = fmaf(-a4.w, col[m + 3], acc3);
-        }
-        col[i] = (acc0 + acc1) + (acc2 + acc3);
-      }
-      // column j of T -> fp16 tile [t][s] (K-major B operand of (b), (c))
-      __half* tt = reinterpret_cast<__half*>(sm + OFF_T);
-#pragma unroll
-      for (int i = 0; i < kC; ++i)
-        *reinterpret_cast<__half*>(sm + OFF_T + tc::sw128_off(i, j)) = __float2half_rn(col[i]);
-      (void)tt;
-    } else {
-      // ---- scaled copies (other 6 warps): gQ (in place), Kt (new), gK (in place)
-      for (int idx = tid - 64; idx < 2048; idx += kThr - 64) {
+      // RAW (row-major input dtype) -> fp16 swizzled tiles; rows past the end are zero
+      for (int idx = p; idx < 3 * 1024; idx += 128) {
         const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
         const int half = ch >> 3, cc = ch & 7;
-        if (m == 0) {
-          uint4* pp = reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 + tc::sw128_chunk(t, cc));
-          *pp = scale8<Op>(*pp, sGam[t]);
-        } else {
-          uint4* pp =
-              reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc));
-          const uint4 raw = *pp;
-          *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
-              scale8<Op>(raw, sKts[t]);
-          *pp = scale8<Op>(raw, sGamP[t]);
-        }
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (t < nvalid)
+          val = to_op8<T>(
+              *reinterpret_cast<const uint4*>(sm + OFF_RAW + m * 16384 + t * 256 + ch * 16));
+        uint32_t off;
+        if (m == 0) off = OFF_QK + half * 16384 + tc::sw128_chunk(t, cc);
+        else if (m == 1) off = OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc);
+        else off = OFF_V + half * 8192 + tc::sw128_chunk(t, cc);
+        *reinterpret_cast<uint4*>(sm + off) = val;
       }
-    }
-    tc::fence_proxy_async();
-    cta_sync_tc();
-    // ---- (b) W^T = (gK)^T T^T,  (c) U^T = V^T T^T
-    if (tid == 0) {
-      constexpr uint32_t id_mn = tc::idesc_f16(128, 64, BF, true, false);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint64_t dt = tc::desc_sw128(sb + OFF_T + ks * 32, 16, 1024);
-        const uint64_t dk = tc::desc_sw128(sb + OFF_QK + 8192 + ks * 2048, 16384, 1024);
-        const uint64_t dv = tc::desc_sw128(sb + OFF_V + ks * 2048, 8192, 1024);
-        tc::mma_f16(tm + TM_W, dk, dt, id_mn, ks > 0);
-        tc::mma_f16(tm + TM_U, dv, dt, id_mn, ks > 0);
+      tc::fence_proxy_async();
+      gsync();
+      if (p == 0 && c + 1 < nchunks) issue_raw(c + 1);
+      if (p < 64) {
+        float* sGam = reinterpret_cast<float*>(G0 + G_GAM);
+        float* sGamP = reinterpret_cast<float*>(G0 + G_GAMP);
+        float* sKts = reinterpret_cast<float*>(G0 + G_KTS);
+        float* sSB = reinterpret_cast<float*>(G0 + G_SB);
+        sSB[p] = (sNeg[p] & 1) ? -sBeta[p] : sBeta[p];
+        sGam[p] = gt.ratio(p, -1);
+        sGamP[p] = p > 0 ? gt.ratio(p - 1, -1) : 1.f;
+        sKts[p] = gt.ratio(kC - 1, p) * sBeta[p];
+        if (p == 0) *reinterpret_cast<float*>(G0 + G_GC) = gt.ratio(kC - 1, -1);
       }
-      tc::mma_commit(mbar);
-    }
-    mma_wait();
-    if (*s_abort) break;
-
-    // ---- -W^T -> bf16 tile [j][t] (MN-major B operand of (d))
-    {
-      uint32_t r[32];
-      tc::tmem_ld32(tm_lane + TM_W + 32 * colh, r);
-      tc::tmem_wait_ld();
-      const int j = 32 * quad + lane;
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint4 pk;
-        pk.x = pack2<Op>(-__uint_as_float(r[8 * c4 + 0]), -__uint_as_float(r[8 * c4 + 1]));
-        pk.y = pack2<Op>(-__uint_as_float(r[8 * c4 + 2]), -__uint_as_float(r[8 * c4 + 3]));
-        pk.z = pack2<Op>(-__uint_as_float(r[8 * c4 + 4]), -__uint_as_float(r[8 * c4 + 5]));
-        pk.w = pack2<Op>(-__uint_as_float(r[8 * c4 + 6]), -__uint_as_float(r[8 * c4 + 7]));
-        *reinterpret_cast<uint4*>(sm + OFF_WT + tc::sw128_chunk(j, 4 * colh + c4)) = pk;
-      }
-    }
-    tc::fence_proxy_async();
-    cta_sync_tc();
-
-    // ---- (d) U^T += S (-W)^T,  (e) O^T = S (gQ)^T
-    if (state_nz) {
-      if (tid == 0) {
-        constexpr uint32_t id_d = tc::idesc_f16(128, 64, BF, false, true);
-        constexpr uint32_t id_e = tc::idesc_f16(128, 64, BF, false, false);
+      // ---- (a) [Q;K] K^T -> QK[b]
+      if (p == 0) {
+        constexpr uint32_t id_a = tc::idesc_f16(128, 64, BF, false, false);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t h = ks >> 2, kk = ks & 3;
-          const uint64_t ds = tc::desc_sw128(sb + OFF_S + h * 16384 + kk * 32, 16, 1024);
-          const uint64_t dw = tc::desc_sw128(sb + OFF_WT + ks * 2048, 8192, 1024);
-          const uint64_t dq = tc::desc_sw128(sb + OFF_QK + h * 16384 + kk * 32, 16, 1024);
-          tc::mma_f16(tm + TM_U, ds, dw, id_d, 1);
-          tc::mma_f16(tm + TM_O, ds, dq, id_e, ks > 0);
+          const uint64_t da = tc::desc_sw128(sb + OFF_QK + h * 16384 + kk * 32, 16, 1024);
+          const uint64_t db = tc::desc_sw128(sb + OFF_QK + h * 16384 + 8192 + kk * 32, 16, 1024);
+          tc::mma_f16(tm + TM_QK0 + 64 * b, da, db, id_a, ks > 0);
         }
-        tc::mma_commit(mbar);
+        tc::mma_commit(bar_pmma);
       }
-      mma_wait();
-      if (*s_abort) break;
-    }
-
-    // ---- U^T -> bf16 tile [i][s]; decay the fp32 state by gamma_{C-1}
-    {
-      uint32_t r[32];
-      tc::tmem_ld32(tm_lane + TM_U + 32 * colh, r);
-      tc::tmem_wait_ld();
-      const int i = 32 * quad + lane;
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint4 pk;
-        pk.x = pack2<Op>(__uint_as_float(r[8 * c4 + 0]), __uint_as_float(r[8 * c4 + 1]));
-        pk.y = pack2<Op>(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
-        pk.z = pack2<Op>(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
-        pk.w = pack2<Op>(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
-        *reinterpret_cast<uint4*>(sm + OFF_UT + tc::sw128_chunk(i, 4 * colh + c4)) = pk;
-      }
-      if (state_nz) {
-        const float gc = *s_gc;
+      if (pmma_wait()) break;
+      // ---- A (rows 64-127 of QK[b]): A[t][s] = ratio(t-1,s) beta_s (k_t . k_s), s < t
+      if (quad >= 2) {
+        const int t = row - 64, tr = t - 1;
+        const float lt = tr >= 0 ? sLc[tr] : 0.f;
+        const int zr = tr >= 0 ? sZ[tr] : -1;
+        const float sg = (tr >= 0 && (sNeg[tr] & 1)) ? -1.f : 1.f;
+        const float* sSB = reinterpret_cast<const float*>(G0 + G_SB);
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          const uint32_t col = TM_S + 64 * colh + 32 * hf;
-          tc::tmem_ld32(tm_lane + col, r);
+          uint32_t r[32];
+          tc::tmem_ld32(tm_lane + TM_QK0 + 64 * b + 32 * hf, r);
           tc::tmem_wait_ld();
+          float pv[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * gc);
-          tc::tmem_st32(tm_lane + col, r);
+          for (int j = 0; j < 32; ++j) {
+            const int s = 32 * hf + j;
+            const bool on = (s <= tr) && (zr <= s);
+            pv[j] = on ? sg * sSB[s] * ex2(lt - sLc[s]) * __uint_as_float(r[j]) : 0.f;
+          }
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4)
+            *reinterpret_cast<float4*>(sA + t * kAStride + 32 * hf + 4 * j4) =
+                make_float4(pv[4 * j4], pv[4 * j4 + 1], pv[4 * j4 + 2], pv[4 * j4 + 3]);
         }
-        tc::tmem_wait_st();
       }
-    }
-    tc::fence_proxy_async();
-    cta_sync_tc();
-
-    // ---- (f) O^T += U^T P^T,  (g) S (+)= U^T Kt
-    if (tid == 0) {
-      constexpr uint32_t id_f = tc::idesc_f16(128, 64, BF, false, false);
-      constexpr uint32_t id_g = tc::idesc_f16(128, 128, BF, false, true);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint64_t du = tc::desc_sw128(sb + OFF_UT + ks * 32, 16, 1024);
-        const uint64_t dp = tc::desc_sw128(sb + OFF_P + ks * 32, 16, 1024);
-        const uint64_t dk = tc::desc_sw128(sb + OFF_KT + ks * 2048, 8192, 1024);
-        tc::mma_f16(tm + TM_O, du, dp, id_f, (state_nz || ks > 0) ? 1u : 0u);
-        tc::mma_f16(tm + TM_S, du, dk, id_g, (state_nz || ks > 0) ? 1u : 0u);
+      // gQ, Kt and T overwrite chain inputs of chunk c - 1: wait for its last MMAs
+      if (c >= 1) {
+        if (gwait(bar_b2, (uint32_t)((c - 1) & 1))) break;
+      } else {
+        gsync();
       }
-      tc::mma_commit(mbar);
-    }
-    mma_wait();
-    if (*s_abort) break;
-    state_nz = true;
-
-    // ---- outputs: O^T -> o rows (staged row-major), state -> bf16 operand tile
-    {
-      uint32_t r[32];
-      tc::tmem_ld32(tm_lane + TM_O + 32 * colh, r);
-      tc::tmem_wait_ld();
-      const int i = 32 * quad + lane;
-      T* so = reinterpret_cast<T*>(sm + OFF_UT);
+      if (p < 64) {
+        // ---- T = (I + A)^-1, one column per thread (A has zeros on/above the diagonal)
+        const int j = p;
+        float col[kC];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) so[(32 * colh + j) * kD + i] = from_f<T>(__uint_as_float(r[j]));
+        for (int i = 0; i < kC; ++i) col[i] = 0.f;
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+          float acc0 = (i == j) ? 1.f : 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+#pragma unroll
+          for (int m = 0; m < i; m += 4) {
+            const float4 a4 = *reinterpret_cast<const float4*>(sA + i * kAStride + m);
+            acc0 = fmaf(-a4.x, col[m], acc0);
+            acc1 = fmaf(-a4.y, col[m + 1], acc1);
+            acc2 = fmaf(-a4.z, col[m + 2], acc2);
+            acc3 = fmaf(-a4.w, col[m + 3], acc3);
+          }
+          col[i] = (acc0 + acc1) + (acc2 + acc3);
+        }
+        // T -> fp16 tile [t][s] in the first half of the W^T buffer
+#pragma unroll
+        for (int i = 0; i < kC; ++i)
+          *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(i, j)) = __float2half_rn(col[i]);
+      } else {
+        // ---- scaled copies: gQ -> GQ, Kt -> KT, gK in place
+        const float* sGam = reinterpret_cast<const float*>(G0 + G_GAM);
+        const float* sGamP = reinterpret_cast<const float*>(G0 + G_GAMP);
+        const float* sKts = reinterpret_cast<const float*>(G0 + G_KTS);
+        for (int idx = p - 64; idx < 2048; idx += 64) {
+          const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
+          const int half = ch >> 3, cc = ch & 7;
+          if (m == 0) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(sm + OFF_QK + half * 16384 +
+                                                              tc::sw128_chunk(t, cc));
+            *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
+                scale8<Op>(raw, sGam[t]);
+          } else {
+            uint4* pp = reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 +
+                                                 tc::sw128_chunk(64 + t, cc));
+            const uint4 raw = *pp;
+            *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
+                scale8<Op>(raw, sKts[t]);
+            *pp = scale8<Op>(raw, sGamP[t]);
+          }
+        }
+      }
+      tc::fence_proxy_async();
+      gsync();
+      // ---- (b) W^T = (gK)^T T^T -> W,  (c) U0^T = V^T T^T -> U[b]
+      if (p == 0) {
+        constexpr uint32_t id_mn = tc::idesc_f16(128, 64, BF, true, false);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t dt = tc::desc_sw128(sb + OFF_WT + ks * 32, 16, 1024);
+          const uint64_t dk = tc::desc_sw128(sb + OFF_QK + 8192 + ks * 2048, 16384, 1024);
+          const uint64_t dv = tc::desc_sw128(sb + OFF_V + ks * 2048, 8192, 1024);
+          tc::mma_f16(tm + TM_W, dk, dt, id_mn, ks > 0);
+          tc::mma_f16(tm + TM_U0 + 64 * b, dv, dt, id_mn, ks > 0);
+        }
+        tc::mma_commit(bar_pmma);
+      }
+      if (pmma_wait()) break;
+      // ---- -W^T -> fp16 tile [j][t] (overwrites T, consumed by (b),(c))
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        tc::tmem_ld32(tm_lane + TM_S + 64 * colh + 32 * hf, r);
+        uint32_t r[32];
+        tc::tmem_ld32(tm_lane + TM_W + 32 * hf, r);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint4 pk;
+          pk.x = pack2<Op>(-__uint_as_float(r[8 * c4 + 0]), -__uint_as_float(r[8 * c4 + 1]));
+          pk.y = pack2<Op>(-__uint_as_float(r[8 * c4 + 2]), -__uint_as_float(r[8 * c4 + 3]));
+          pk.z = pack2<Op>(-__uint_as_float(r[8 * c4 + 4]), -__uint_as_float(r[8 * c4 + 5]));
+          pk.w = pack2<Op>(-__uint_as_float(r[8 * c4 + 6]), -__uint_as_float(r[8 * c4 + 7]));
+          *reinterpret_cast<uint4*>(sm + OFF_WT + tc::sw128_chunk(row, 4 * hf + c4)) = pk;
+        }
+      }
+      tc::fence_proxy_async();
+      gsync();
+      if (p == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar_prep))
+                               : "memory");
+    }
+    // an abort can leave one bulk copy in flight: let it land before exiting
+    if (*s_abort && p == 0) tc::mbar_wait(bar_raw, raw_phase, kWaitLimit);
+  } else {
+    // =====================================================================
+    // chain warps: the state-dependent part of each chunk
+    // =====================================================================
+    const int i = row;  // state row / value channel
+    bool state_nz = false;
+    if (h0) {
+      const float* hh = h0 + head * kD * kD;
+#pragma unroll
+      for (int hq = 0; hq < 4; ++hq) {
+        const int j0 = 32 * hq;
+        uint32_t r[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(hh[i * kD + j0 + j]);
+        tc::tmem_st32(tm_lane + TM_S + j0, r);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint4 pk;
+          pk.x = pack2<Op>(__uint_as_float(r[8 * c4 + 0]), __uint_as_float(r[8 * c4 + 1]));
+          pk.y = pack2<Op>(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
+          pk.z = pack2<Op>(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
+          pk.w = pack2<Op>(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
+          *reinterpret_cast<uint4*>(sm + OFF_S + (hq >> 1) * 16384 +
+                                    tc::sw128_chunk(i, 4 * (hq & 1) + c4)) = pk;
+        }
+      }
+      tc::tmem_wait_st();
+      tc::fence_proxy_async();
+      state_nz = true;
+    }
+    for (int64_t c = 0; c < nchunks; ++c) {
+      const int b = (int)(c & 1);
+      const uint32_t ph = (uint32_t)(c & 1);
+      const int64_t tok0 = c * kC;
+      const int nvalid = (int)((L - tok0) < kC ? (L - tok0) : kC);
+      const uint8_t* G0 = gtab(b);
+      const float* sLc = reinterpret_cast<const float*>(G0 + G_LC);
+      const int* sZ = reinterpret_cast<const int*>(G0 + G_Z);
+      const int* sNeg = reinterpret_cast<const int*>(G0 + G_NEG);
+      const float* sSB = reinterpret_cast<const float*>(G0 + G_SB);
+      if (gwait(bar_prep, ph)) break;
+      // ---- (d) U^T[b] += S (-W)^T,  (e) O^T = S (gQ)^T   (need the state)
+      if (gt_id == 0) {
+        if (state_nz) {
+          constexpr uint32_t id_d = tc::idesc_f16(128, 64, BF, false, true);
+          constexpr uint32_t id_e = tc::idesc_f16(128, 64, BF, false, false);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t h = ks >> 2, kk = ks & 3;
+            const uint64_t ds = tc::desc_sw128(sb + OFF_S + h * 16384 + kk * 32, 16, 1024);
+            const uint64_t dw = tc::desc_sw128(sb + OFF_WT + ks * 2048, 8192, 1024);
+            const uint64_t dq = tc::desc_sw128(sb + OFF_GQ + h * 8192 + kk * 32, 16, 1024);
+            tc::mma_f16(tm + TM_U0 + 64 * b, ds, dw, id_d, 1);
+            tc::mma_f16(tm + TM_O, ds, dq, id_e, ks > 0);
+          }
+          tc::mma_commit(bar_b1);
+        } else {
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar_b1))
+                       : "memory");
+        }
+      }
+      // ---- P (rows 0-63 of QK[b]) while (d),(e) run: P[t][s] = ratio(t,s) beta_s (q_t . k_s)
+      if (quad < 2) {
+        const int t = row;
+        const float lt = sLc[t];
+        const int zr = sZ[t];
+        const float sg = (sNeg[t] & 1) ? -1.f : 1.f;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t r[32];
+          tc::tmem_ld32(tm_lane + TM_QK0 + 64 * b + 32 * hf, r);
+          tc::tmem_wait_ld();
+          float pv[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int s = 32 * hf + j;
+            const bool on = (s <= t) && (zr <= s);
+            pv[j] = on ? sg * sSB[s] * ex2(lt - sLc[s]) * __uint_as_float(r[j]) : 0.f;
+          }
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint4 pk;
+            pk.x = pack2<Op>(pv[8 * c4 + 0], pv[8 * c4 + 1]);
+            pk.y = pack2<Op>(pv[8 * c4 + 2], pv[8 * c4 + 3]);
+            pk.z = pack2<Op>(pv[8 * c4 + 4], pv[8 * c4 + 5]);
+            pk.w = pack2<Op>(pv[8 * c4 + 6], pv[8 * c4 + 7]);
+            *reinterpret_cast<uint4*>(sm + OFF_P + tc::sw128_chunk(t, 4 * hf + c4)) = pk;
+          }
+        }
+      }
+      tc::fence_proxy_async();
+      if (gwait(bar_b1, ph)) break;
+      // ---- U^T -> fp16 tile [i][s]; decay the fp32 state by gamma_{C-1}
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t r[32];
+        tc::tmem_ld32(tm_lane + TM_U0 + 64 * b + 32 * hf, r);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
@@ -518,42 +561,97 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
           pk.y = pack2<Op>(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
           pk.z = pack2<Op>(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
           pk.w = pack2<Op>(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
-          *reinterpret_cast<uint4*>(sm + OFF_S + colh * 16384 +
-                                    tc::sw128_chunk(i, 4 * hf + c4)) = pk;
+          *reinterpret_cast<uint4*>(sm + OFF_UT + tc::sw128_chunk(i, 4 * hf + c4)) = pk;
         }
       }
-    }
-    tc::fence_proxy_async();
-    cta_sync_tc();
-    for (int e = tid; e < nvalid * 16; e += kThr) {
-      const int t = e >> 4, ch = e & 15;
-      st_global_v4(oh + (tok0 + t) * kD + ch * 8,
-                   *reinterpret_cast<const uint4*>(sm + OFF_UT + t * 256 + ch * 16));
-    }
-    // (next chunk's loads overwrite QK/V/KT only after the barrier that follows them)
-  }
-
-  // an abort can leave one bulk copy in flight: let it land before the CTA exits
-  if (*s_abort && tid == 0) tc::mbar_wait(rawbar, rphase, kWaitLimit);
-
-  // ---- final state
-  if (hT && !*s_abort) {
-    float* hh = hT + head * kD * kD;
-    const int i = 32 * quad + lane;
-    for (int hf = 0; hf < 2; ++hf) {
-      uint32_t r[32];
-      const int j0 = 64 * colh + 32 * hf;
       if (state_nz) {
-        tc::tmem_ld32(tm_lane + TM_S + j0, r);
-        tc::tmem_wait_ld();
-      } else {
+        const float gc = *reinterpret_cast<const float*>(G0 + G_GC);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
+        for (int hq = 0; hq < 4; ++hq) {
+          uint32_t r[32];
+          tc::tmem_ld32(tm_lane + TM_S + 32 * hq, r);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * gc);
+          tc::tmem_st32(tm_lane + TM_S + 32 * hq, r);
+        }
+        tc::tmem_wait_st();
       }
+      tc::fence_proxy_async();
+      gsync();
+      // ---- (f) O^T += U^T P^T,  (g) S (+)= U^T Kt
+      if (gt_id == 0) {
+        constexpr uint32_t id_f = tc::idesc_f16(128, 64, BF, false, false);
+        constexpr uint32_t id_g = tc::idesc_f16(128, 128, BF, false, true);
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4)
-        *reinterpret_cast<uint4*>(hh + i * kD + j0 + 4 * j4) =
-            make_uint4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t du = tc::desc_sw128(sb + OFF_UT + ks * 32, 16, 1024);
+          const uint64_t dp = tc::desc_sw128(sb + OFF_P + ks * 32, 16, 1024);
+          const uint64_t dk = tc::desc_sw128(sb + OFF_KT + ks * 2048, 8192, 1024);
+          tc::mma_f16(tm + TM_O, du, dp, id_f, (state_nz || ks > 0) ? 1u : 0u);
+          tc::mma_f16(tm + TM_S, du, dk, id_g, (state_nz || ks > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(bar_b2);
+      }
+      if (gwait(bar_b2, ph)) break;
+      state_nz = true;
+      // ---- O^T -> staging [t][i] (U^T buffer, consumed), state -> fp16 operand copy
+      {
+        uint32_t r[32];
+        T* so = reinterpret_cast<T*>(sm + OFF_UT);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          tc::tmem_ld32(tm_lane + TM_O + 32 * hf, r);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) so[(32 * hf + j) * kD + i] = from_f<T>(__uint_as_float(r[j]));
+        }
+#pragma unroll
+        for (int hq = 0; hq < 4; ++hq) {
+          tc::tmem_ld32(tm_lane + TM_S + 32 * hq, r);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint4 pk;
+            pk.x = pack2<Op>(__uint_as_float(r[8 * c4 + 0]), __uint_as_float(r[8 * c4 + 1]));
+            pk.y = pack2<Op>(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
+            pk.z = pack2<Op>(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
+            pk.w = pack2<Op>(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
+            *reinterpret_cast<uint4*>(sm + OFF_S + (hq >> 1) * 16384 +
+                                      tc::sw128_chunk(i, 4 * (hq & 1) + c4)) = pk;
+          }
+        }
+      }
+      tc::fence_proxy_async();
+      gsync();
+      for (int e = gt_id; e < nvalid * 16; e += 128) {
+        const int t = e >> 4, ch = e & 15;
+        st_global_v4(oh + (tok0 + t) * kD + ch * 8,
+                     *reinterpret_cast<const uint4*>(sm + OFF_UT + t * 256 + ch * 16));
+      }
+      gsync();  // staging read before the next chunk's U^T overwrites it
+      if (gt_id == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar_done + b))
+                     : "memory");
+    }
+    // ---- final state
+    if (hT && !*s_abort) {
+      float* hh = hT + head * kD * kD;
+#pragma unroll
+      for (int hq = 0; hq < 4; ++hq) {
+        uint32_t r[32];
+        if (state_nz) {
+          tc::tmem_ld32(tm_lane + TM_S + 32 * hq, r);
+          tc::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4)
+          *reinterpret_cast<uint4*>(hh + i * kD + 32 * hq + 4 * j4) =
+              make_uint4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
+      }
     }
   }
   tc::fence_before_sync();

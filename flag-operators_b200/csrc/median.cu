@@ -158,7 +158,7 @@ template <int RG, int NI, int VW, int DIG0, int DIGL>
 using GroupSmemOf = GroupSmem<RG, RG * 32 * NI * VW, (1 << (DIG0 > DIGL ? DIG0 : DIGL)) / 2>;
 
 template <typename T, int RG, int NI, int VW, int DIG0, int DIGL, int GPC>
-__global__ void __launch_bounds__(GPC * RG * 32)
+__global__ void __launch_bounds__(GPC * RG * 32, 3)
 median_group_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restrict__ idxs,
                     int64_t M, int N) {
   using Tr = KeyTraits<T>;
@@ -172,34 +172,53 @@ median_group_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __re
   const int k = (N - 1) / 2;
   constexpr int SH0 = 32 - DIG0;
 
-  for (int64_t row = (int64_t)blockIdx.x * GPC + g; row < M; row += (int64_t)gridDim.x * GPC) {
+  // The next row's raw data is loaded into registers while the current row is
+  // selected (rows are ~8 KiB; the load latency is otherwise exposed per row).
+  constexpr int RN = VW > 1 ? 1 : VW;
+  uint4 rv[NI];           // 16-byte vectors (VW > 1)
+  T rs[NI][RN];           // scalars (VW == 1)
+  auto load_row = [&](int64_t rrow) {
+    if (rrow >= M) return;
+    const T* xx = x + rrow * (int64_t)N;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int base = ((i * RG + w) * 32 + lane) * VW;
+      if (VW > 1) {
+        rv[i] = (base + VW <= N) ? ld_global_stream_v4(xx + base) : make_uint4(0, 0, 0, 0);
+      } else {
+#pragma unroll
+        for (int c = 0; c < RN; ++c) rs[i][c] = (base + c < N) ? xx[base + c] : T(0);
+      }
+    }
+  };
+  const int64_t row0 = (int64_t)blockIdx.x * GPC + g;
+  const int64_t rstep = (int64_t)gridDim.x * GPC;
+  load_row(row0);
+
+  for (int64_t row = row0; row < M; row += rstep) {
     const T* xr = x + row * (int64_t)N;
     uint32_t key[NI][VW];
     bool nan_seen = false;
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
       const int base = ((i * RG + w) * 32 + lane) * VW;
-      if (VW > 1 && base + VW <= N) {
-        const uint4 u = ld_global_stream_v4(xr + base);
-        const T* e = reinterpret_cast<const T*>(&u);
+      if (VW > 1) {
+        const T* e = reinterpret_cast<const T*>(&rv[i]);
 #pragma unroll
         for (int c = 0; c < VW; ++c) {
           key[i][c] = Tr::key(e[c]);
-          nan_seen |= Tr::isnan_(e[c]);
+          nan_seen |= (base + c < N) && Tr::isnan_(e[c]);
         }
       } else {
 #pragma unroll
         for (int c = 0; c < VW; ++c) {
-          if (base + c < N) {
-            const T v = xr[base + c];
-            key[i][c] = Tr::key(v);
-            nan_seen |= Tr::isnan_(v);
-          } else {
-            key[i][c] = 0;
-          }
+          const T vv = rs[i][c < RN ? c : 0];
+          key[i][c] = (base + c < N) ? Tr::key(vv) : 0u;
+          nan_seen |= (base + c < N) && Tr::isnan_(vv);
         }
       }
     }
+    load_row(row + rstep);
     if (t == 0) {
       S.first_nan = ~0ull;
       S.ncand = 0;
