@@ -51,9 +51,16 @@ __device__ __forceinline__ void ms_add_vec(MS& st, float& rsum, const float* f, 
     st.m = lm;
   }
   if (st.m != -INFINITY) {
+    // tree sum of the vector, then one add into the running sum (short dependency chain)
     const float mb = st.m * kLog2e;
+    float e[E];
 #pragma unroll
-    for (int i = 0; i < E; ++i) st.s += fast_exp2(fmaf(f[i], kLog2e, -mb));
+    for (int i = 0; i < E; ++i) e[i] = fast_exp2(fmaf(f[i], kLog2e, -mb));
+#pragma unroll
+    for (int w = 1; w < E; w <<= 1)
+#pragma unroll
+      for (int i = 0; i + w < E; i += 2 * w) e[i] += e[i + w];
+    st.s += e[0];
   }
   if (ls) {
 #pragma unroll
@@ -146,10 +153,10 @@ __device__ __forceinline__ void row_grad(const T* __restrict__ p, T* __restrict_
   const bool vec = ((ap & 15) == (ag & 15)) && (ap % sizeof(T)) == 0;
   int64_t head = vec ? (int64_t)(((16 - (ap & 15)) & 15) / sizeof(T)) : n;
   if (head > n) head = n;
+  // the one-hot term of the target column is added by fix_target() afterwards
   auto one = [&](int64_t j, float x) -> float {
-    float v = (scale == 0.f) ? 0.f : scale * fast_exp2(fmaf(x, kLog2e, -lb)) - se;
-    if (j + col0 == t) v -= scale * one_m_e;
-    return v;
+    (void)j;
+    return (scale == 0.f) ? 0.f : scale * fast_exp2(fmaf(x, kLog2e, -lb)) - se;
   };
   for (int64_t j = threadIdx.x; j < head; j += blockDim.x)
     g[j] = from_f<T>(one(j, scale == 0.f ? 0.f : to_f<T>(p[j])));
@@ -184,6 +191,23 @@ __device__ __forceinline__ void row_grad(const T* __restrict__ p, T* __restrict_
   }
   for (int64_t j = head + nvec * E + threadIdx.x; j < n; j += blockDim.x)
     g[j] = from_f<T>(one(j, scale == 0.f ? 0.f : to_f<T>(p[j])));
+}
+
+// Rewrites the target element of a gradient row with its one-hot term.  Called
+// by every thread after row_grad; the CTA barrier orders it after the vector
+// store that wrote the same element.
+template <typename T>
+__device__ __forceinline__ void fix_target(const T* __restrict__ p, T* __restrict__ g, int64_t n,
+                                           int64_t col0, int64_t t, float lse, float scale,
+                                           float eps_v, float one_m_e) {
+  __syncthreads();
+  const int64_t j = t - col0;
+  if (threadIdx.x == 0 && scale != 0.f && j >= 0 && j < n) {
+    const float x = to_f<T>(p[j]);
+    const float v = scale * fast_exp2(fmaf(x, kLog2e, -lse * kLog2e)) - scale * eps_v -
+                    scale * one_m_e;
+    g[j] = from_f<T>(v);
+  }
 }
 
 // n_valid = #(target != ignore_index), written as float.
@@ -242,6 +266,8 @@ ce_fwd_kernel(const T* __restrict__ logits, const int64_t* __restrict__ target,
       if (valid && reduction == FO_RED_MEAN) scale = 1.f / *n_valid;
       row_grad<T>(row, dlogits + b * V, V, 0, t, lse, scale, LS ? eps / (float)V : 0.f,
                   1.f - eps);
+      fix_target<T>(row, dlogits + b * V, V, 0, t, lse, scale, LS ? eps / (float)V : 0.f,
+                    1.f - eps);
     }
   }
 }
@@ -274,6 +300,8 @@ ce_bwd_kernel(const T* __restrict__ logits, const int64_t* __restrict__ target,
     }
     row_grad<T>(logits + b * ld, dlogits + b * Vn, Vn, col0, t, lse[b], scale,
                 LS ? eps / (float)V : 0.f, 1.f - eps);
+    fix_target<T>(logits + b * ld, dlogits + b * Vn, Vn, col0, t, lse[b], scale,
+                  LS ? eps / (float)V : 0.f, 1.f - eps);
   }
 }
 
@@ -369,7 +397,9 @@ int ce_fwd_t(const void* logits, const int64_t* target, float* loss_rows, float*
              int64_t ignore_index, float eps, int reduction, cudaStream_t st) {
   ce_count_valid_kernel<<<1, 1024, 0, st>>>(target, B, ignore_index, n_valid);
   if (int rc = check_launch("ce_count_valid_kernel")) return rc;
-  const int grid = grid_rows(B, 4);
+  // with the gradient fused, pass 2 re-reads each row from L2: keep the rows in
+  // flight (CTAs x 250 KB for V = 128K bf16) well inside the 126 MB L2
+  const int grid = grid_rows(B, dlogits ? 2 : 4);
   if (eps != 0.f)
     ce_fwd_kernel<T, true><<<grid, kThreads, 0, st>>>((const T*)logits, target, loss_rows, lse,
                                                       (T*)dlogits, n_valid, B, V, ld,

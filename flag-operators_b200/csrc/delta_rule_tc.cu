@@ -87,31 +87,53 @@ __device__ __forceinline__ uint4 to_op8(uint4 u) {
   if constexpr (std::is_same<T, __half>::value) {
     return u;
   } else {
-    const T* e = reinterpret_cast<const T*>(&u);
-    uint4 r;
-    __half* h = reinterpret_cast<__half*>(&r);
+    // a bf16 pair in one word: low half << 16 and high half & 0xffff0000 are its floats
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = __float2half_rn(to_f<T>(e[i]));
-    return r;
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(__uint_as_float(w[i] << 16),
+                                          __uint_as_float(w[i] & 0xffff0000u));
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return u;
   }
 }
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
-  T x = from_f<T>(a), y = from_f<T>(b);
-  return (uint32_t)(*reinterpret_cast<uint16_t*>(&x)) |
-         ((uint32_t)(*reinterpret_cast<uint16_t*>(&y)) << 16);
+  if constexpr (std::is_same<T, __half>::value) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
 }
 
-// element-wise scale of a 16-byte chunk of 8 16-bit values
-template <typename T>
-__device__ __forceinline__ uint4 scale8(uint4 u, float s) {
-  T* e = reinterpret_cast<T*>(&u);
-  uint4 r;
-  uint32_t* rr = reinterpret_cast<uint32_t*>(&r);
+// packed fp32x2 arithmetic (one instruction for two lanes of a float2)
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&r);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
+// 8 fp16 values times a scale (HMUL2; the product is rounded to fp16 as the
+// operand tile would be anyway)
+__device__ __forceinline__ uint4 scale8h(uint4 u, __half2 s) {
+  __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) rr[i] = pack2<Op>(to_f<T>(e[2 * i]) * s, to_f<T>(e[2 * i + 1]) * s);
-  return r;
+  for (int i = 0; i < 4; ++i) h[i] = __hmul2(h[i], s);
+  return u;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -299,19 +321,30 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         sZ[p] = max(sZ[p], sZ[31]);
         sNeg[p] += sNeg[31];
       }
-      // RAW (row-major input dtype) -> fp16 swizzled tiles; rows past the end are zero
-      for (int idx = p; idx < 3 * 1024; idx += 128) {
-        const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
-        const int half = ch >> 3, cc = ch & 7;
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (t < nvalid)
-          val = to_op8<T>(
-              *reinterpret_cast<const uint4*>(sm + OFF_RAW + m * 16384 + t * 256 + ch * 16));
-        uint32_t off;
-        if (m == 0) off = OFF_QK + half * 16384 + tc::sw128_chunk(t, cc);
-        else if (m == 1) off = OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc);
-        else off = OFF_V + half * 8192 + tc::sw128_chunk(t, cc);
-        *reinterpret_cast<uint4*>(sm + off) = val;
+      // RAW (row-major input dtype) -> fp16 swizzled tiles; rows past the end are
+      // zero.  24 chunks of 16 bytes per thread, 8 loads in flight at a time.
+#pragma unroll 1
+      for (int base = p; base < 3 * 1024; base += 8 * 128) {
+        uint4 val[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int idx = base + u * 128;
+          const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
+          val[u] = (t < nvalid) ? *reinterpret_cast<const uint4*>(sm + OFF_RAW + m * 16384 +
+                                                                  t * 256 + ch * 16)
+                                : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int idx = base + u * 128;
+          const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
+          const int half = ch >> 3, cc = ch & 7;
+          uint32_t off;
+          if (m == 0) off = OFF_QK + half * 16384 + tc::sw128_chunk(t, cc);
+          else if (m == 1) off = OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc);
+          else off = OFF_V + half * 8192 + tc::sw128_chunk(t, cc);
+          *reinterpret_cast<uint4*>(sm + off) = to_op8<T>(val[u]);
+        }
       }
       tc::fence_proxy_async();
       gsync();
@@ -357,7 +390,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
           for (int j = 0; j < 32; ++j) {
             const int s = 32 * hf + j;
             const bool on = (s <= tr) && (zr <= s);
-            pv[j] = on ? sg * sSB[s] * ex2(lt - sLc[s]) * __uint_as_float(r[j]) : 0.f;
+            pv[j] = on ? -sg * sSB[s] * ex2(lt - sLc[s]) * __uint_as_float(r[j]) : 0.f;
           }
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4)
@@ -372,33 +405,37 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         gsync();
       }
       if (p < 64) {
-        // ---- T = (I + A)^-1, one column per thread (A has zeros on/above the diagonal)
+        // ---- T = (I + A)^-1, one column per thread.  sA holds -A (zero on and
+        // above the diagonal), so T[i][j] = [i == j] + sum_{m<i} sA[i][m] T[m][j];
+        // the column is held as float2 pairs updated with packed fp32x2 FMAs.
         const int j = p;
-        float col[kC];
+        float2 col[kC / 2];
 #pragma unroll
-        for (int i = 0; i < kC; ++i) col[i] = 0.f;
+        for (int i = 0; i < kC / 2; ++i) col[i] = make_float2(0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < kC; ++i) {
-          float acc0 = (i == j) ? 1.f : 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+          float2 acc0 = make_float2((i == j) ? 1.f : 0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int m = 0; m < i; m += 4) {
             const float4 a4 = *reinterpret_cast<const float4*>(sA + i * kAStride + m);
-            acc0 = fmaf(-a4.x, col[m], acc0);
-            acc1 = fmaf(-a4.y, col[m + 1], acc1);
-            acc2 = fmaf(-a4.z, col[m + 2], acc2);
-            acc3 = fmaf(-a4.w, col[m + 3], acc3);
+            acc0 = fma2(make_float2(a4.x, a4.y), col[m / 2], acc0);
+            acc1 = fma2(make_float2(a4.z, a4.w), col[m / 2 + 1], acc1);
           }
-          col[i] = (acc0 + acc1) + (acc2 + acc3);
+          const float vv = (acc0.x + acc0.y) + (acc1.x + acc1.y);
+          if (i & 1) col[i / 2].y = vv;
+          else col[i / 2].x = vv;
         }
         // T -> fp16 tile [t][s] in the first half of the W^T buffer
 #pragma unroll
         for (int i = 0; i < kC; ++i)
-          *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(i, j)) = __float2half_rn(col[i]);
+          *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(i, j)) =
+              __float2half_rn((i & 1) ? col[i / 2].y : col[i / 2].x);
       } else {
         // ---- scaled copies: gQ -> GQ, Kt -> KT, gK in place
         const float* sGam = reinterpret_cast<const float*>(G0 + G_GAM);
         const float* sGamP = reinterpret_cast<const float*>(G0 + G_GAMP);
         const float* sKts = reinterpret_cast<const float*>(G0 + G_KTS);
+#pragma unroll 2
         for (int idx = p - 64; idx < 2048; idx += 64) {
           const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
           const int half = ch >> 3, cc = ch & 7;
@@ -406,14 +443,14 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
             const uint4 raw = *reinterpret_cast<const uint4*>(sm + OFF_QK + half * 16384 +
                                                               tc::sw128_chunk(t, cc));
             *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
-                scale8<Op>(raw, sGam[t]);
+                scale8h(raw, __float2half2_rn(sGam[t]));
           } else {
             uint4* pp = reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 +
                                                  tc::sw128_chunk(64 + t, cc));
             const uint4 raw = *pp;
             *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
-                scale8<Op>(raw, sKts[t]);
-            *pp = scale8<Op>(raw, sGamP[t]);
+                scale8h(raw, __float2half2_rn(sKts[t]));
+            *pp = scale8h(raw, __float2half2_rn(sGamP[t]));
           }
         }
       }
@@ -571,8 +608,13 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
           uint32_t r[32];
           tc::tmem_ld32(tm_lane + TM_S + 32 * hq, r);
           tc::tmem_wait_ld();
+          const float2 g2 = make_float2(gc, gc);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * gc);
+          for (int j = 0; j < 32; j += 2) {
+            const float2 m2 = mul2(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), g2);
+            r[j] = __float_as_uint(m2.x);
+            r[j + 1] = __float_as_uint(m2.y);
+          }
           tc::tmem_st32(tm_lane + TM_S + 32 * hq, r);
         }
         tc::tmem_wait_st();

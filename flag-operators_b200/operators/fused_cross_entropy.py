@@ -141,6 +141,19 @@ class _ShardedCrossEntropy(torch.autograd.Function):
         return dlogits, None, None, None, None, None, None, None
 
 
+def shard_layout(rank: int, world: int, v_local: int, vocab_offset=None, vocab_size=None):
+    """(first global column of this rank's block, full vocabulary size).
+
+    Default: equal blocks in rank order, V = v_local * world.  Explicit values
+    allow uneven splits; every rank must pass the same vocab_size.
+    """
+    off = rank * v_local if vocab_offset is None else int(vocab_offset)
+    V = v_local * world if vocab_size is None else int(vocab_size)
+    if not (0 <= off and off + v_local <= V):
+        raise ValueError(f"vocabulary block [{off}, {off + v_local}) outside [0, {V})")
+    return off, V
+
+
 def fused_cross_entropy(
     logits: torch.Tensor,
     target: torch.Tensor,
@@ -166,11 +179,8 @@ def fused_cross_entropy(
         raise ValueError(f"label_smoothing must be in [0, 1], got {label_smoothing}")
     if process_group is not None:
         import torch.distributed as dist
-        rank = dist.get_rank(process_group)
-        P = dist.get_world_size(process_group)
-        Vn = logits.shape[1]
-        off = rank * Vn if vocab_offset is None else int(vocab_offset)
-        V = Vn * P if vocab_size is None else int(vocab_size)
+        off, V = shard_layout(dist.get_rank(process_group), dist.get_world_size(process_group),
+                              logits.shape[1], vocab_offset, vocab_size)
         return _ShardedCrossEntropy.apply(logits, target, reduction, ignore_index,
                                           label_smoothing, process_group, off, V)
     return _FusedCrossEntropy.apply(logits, target, reduction, ignore_index, label_smoothing)
