@@ -23,4 +23,6 @@ from .ops import (  # noqa: F401
     fused_cross_entropy,
     fused_cross_entropy_grad,
     delta_rule_forward,
+    ce_shard_stats,
+    ce_shard_combine,
 )

@@ -160,3 +160,41 @@ def delta_rule_forward(q, k, v, beta, g, initial_state=None, output_final_state=
     if output_final_state:
         return o, h
     return o
+
+
+# ---------------------------------------------------------------------------
+# vocabulary-sharded cross-entropy: statement of the sharded algorithm on CPU
+# (used by the multi-process tests to check the host logic and the combine rule;
+# the single-device result it must reproduce is F.cross_entropy above)
+# ---------------------------------------------------------------------------
+def ce_shard_stats(logits_block, target, v_offset, ignore_index=-100):
+    """[B, 4] float64: (row max, sum exp(x - max), target logit if in block else 0, row sum)."""
+    x = _cpu(logits_block).double()
+    t = _cpu(target)
+    m = x.max(dim=1).values
+    s = torch.exp(x - m[:, None]).sum(dim=1)
+    cols = t - v_offset
+    inb = (t != ignore_index) & (cols >= 0) & (cols < x.shape[1])
+    xt = torch.where(inb, x.gather(1, cols.clamp(0, x.shape[1] - 1)[:, None]).squeeze(1),
+                     torch.zeros_like(m))
+    return torch.stack([m, s, xt, x.sum(dim=1)], dim=1)
+
+
+def ce_shard_combine(all_stats, target, V, ignore_index=-100, label_smoothing=0.0,
+                     reduction="mean"):
+    """Combines [P, B, 4] block statistics into the loss, as on one device."""
+    st = _cpu(all_stats).double()
+    t = _cpu(target)
+    m = st[:, :, 0].max(dim=0).values
+    s = (st[:, :, 1] * torch.exp(st[:, :, 0] - m[None, :])).sum(dim=0)
+    lse = m + torch.log(s)
+    xt = st[:, :, 2].sum(dim=0)
+    rowsum = st[:, :, 3].sum(dim=0)
+    valid = t != ignore_index
+    e = label_smoothing
+    loss = torch.where(valid, lse - (1 - e) * xt - e * rowsum / V, torch.zeros_like(lse))
+    if reduction == "none":
+        return loss
+    if reduction == "sum":
+        return loss.sum()
+    return loss.sum() / valid.sum()

@@ -1,0 +1,80 @@
+"""Multi-process (world size 2, gloo, CPU) tests of the vocabulary-sharded
+cross-entropy host logic: block layout, the all_gather of per-row statistics and
+the combine rule reproduce the single-device loss.  The CUDA kernels of the same
+path run in tests/test_multigpu.py on 2 GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from operators.fused_cross_entropy import shard_layout
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, V, uneven, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        g = torch.Generator().manual_seed(5)
+        B = 12
+        logits = torch.randn(B, V, generator=g) * 2
+        target = torch.randint(0, V, (B,), generator=g)
+        target[3] = -100
+        if uneven:
+            bounds = [0, V // 3, V]
+            off, Vfull = shard_layout(rank, world, bounds[rank + 1] - bounds[rank],
+                                      vocab_offset=bounds[rank], vocab_size=V)
+            block = logits[:, bounds[rank]:bounds[rank + 1]]
+        else:
+            vl = V // world
+            off, Vfull = shard_layout(rank, world, vl)
+            block = logits[:, off:off + vl]
+        stats = oracle.ce_shard_stats(block, target, off).float()
+        gathered = [torch.empty_like(stats) for _ in range(world)]
+        dist.all_gather(gathered, stats)
+        all_stats = torch.stack(gathered)
+        res = {}
+        for red in ("none", "mean", "sum"):
+            for ls in (0.0, 0.1):
+                got = oracle.ce_shard_combine(all_stats, target, Vfull, label_smoothing=ls,
+                                              reduction=red)
+                ref = oracle.fused_cross_entropy(logits.double(), target, reduction=red,
+                                                 label_smoothing=ls)
+                res[(red, ls)] = float((got - ref).abs().max())
+        q.put((rank, res))
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("uneven", [False, True])
+def test_vocab_sharded_ce_two_ranks_gloo(uneven):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, 1000, uneven, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, res in out:
+        assert isinstance(res, dict), f"rank {rank} failed: {res}"
+        for k, err in res.items():
+            assert err < 1e-4, (rank, k, err)
+
+
+def test_shard_layout_rules():
+    assert shard_layout(1, 4, 100) == (100, 400)
+    assert shard_layout(0, 2, 30, vocab_offset=0, vocab_size=50) == (0, 50)
+    with pytest.raises(ValueError):
+        shard_layout(3, 4, 100, vocab_size=350)
