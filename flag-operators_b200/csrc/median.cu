@@ -10,17 +10,20 @@
 // Algorithm: radix select on an order-preserving unsigned key
 //   float: key = bits ^ (sign ? 0xffffffff : 0x80000000) after -0.0 -> +0.0
 //   int:   key = bits ^ sign bit
-// in digits of 11 bits from the most significant end.  Each pass histograms the
-// digit of the elements whose higher digits equal the prefix selected so far and
-// picks the bucket holding rank r.  After the last pass the key K of the k-th
-// element is known, and r is its occurrence rank among the elements equal to K;
-// the answer is the r-th such element in index order, found with ballots.
+// Each pass histograms a digit of the elements whose higher digits equal the
+// prefix selected so far and picks the bucket holding rank r.
 //
-// Short rows (N <= 2048): one warp per row.  The row sits in registers (loaded
-// once, 16-byte vectors when the row is 16-byte aligned), the histogram is
-// private to the warp in shared memory as packed 16-bit counters, and no block
-// barrier is needed.  Long rows and the global median: one CTA per row, passes
-// re-read the row (L2 hits for rows that fit in L2).
+// Rows of N <= 2048 (4-byte and smaller types): a group of RG = 1, 2 or 4 warps
+// per row, 16 elements per thread in registers (16-byte vector loads when the
+// row is 16-byte aligned; the next row is loaded while the current one is
+// selected).  One pass over the top log2(512 RG) key bits, compaction of the
+// selected bucket as 32-bit (key << digit bits | index) composites whose order
+// is the stable sort order, and selection among them (rank counting for <= 32,
+// radix passes otherwise).  NaN and infinite keys fall in the histogram's edge
+// bins, so the NaN rule costs nothing per element unless those bins are used.
+// Longer rows, int64 and the global median: one CTA per row, 11-bit digits,
+// passes re-read the row (L2 hits for rows that fit in L2); after the last pass
+// the key of the k-th element is known and the answer is found with ballots.
 #include "common.cuh"
 
 namespace fo {
@@ -37,11 +40,27 @@ template <> struct KeyTraits<float> {
     return u ^ ((uint32_t)((int32_t)u >> 31) | 0x80000000u);
   }
   static __device__ __forceinline__ bool isnan_(float x) { return x != x; }
+  static constexpr bool kHasNan = true;
+  // NaN keys lie above the +inf key (0xff800000) or below the -inf key (0x007fffff)
+  static __device__ __forceinline__ bool key_is_nan(uint32_t k) {
+    return k > 0xff800000u || k < 0x007fffffu;
+  }
+  // +0.0 and -0.0 share one key; the stored element decides the sign of the value
+  static __device__ __forceinline__ bool is_zero_key(uint32_t k) { return k == 0x80000000u; }
+  static __device__ __forceinline__ float from_key(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k ^ 0x80000000u) : ~k);
+  }
 };
 template <> struct KeyTraits<__half> {
   using K = uint32_t;
   static __device__ __forceinline__ K key(__half x) { return KeyTraits<float>::key(__half2float(x)); }
   static __device__ __forceinline__ bool isnan_(__half x) { return __hisnan(x); }
+  static constexpr bool kHasNan = true;
+  static __device__ __forceinline__ bool key_is_nan(uint32_t k) { return KeyTraits<float>::key_is_nan(k); }
+  static __device__ __forceinline__ bool is_zero_key(uint32_t k) { return k == 0x80000000u; }
+  static __device__ __forceinline__ __half from_key(uint32_t k) {
+    return __float2half_rn(KeyTraits<float>::from_key(k));  // exact: the key came from a half
+  }
 };
 template <> struct KeyTraits<__nv_bfloat16> {
   using K = uint32_t;
@@ -49,11 +68,21 @@ template <> struct KeyTraits<__nv_bfloat16> {
     return KeyTraits<float>::key(__bfloat162float(x));
   }
   static __device__ __forceinline__ bool isnan_(__nv_bfloat16 x) { return __hisnan(x); }
+  static constexpr bool kHasNan = true;
+  static __device__ __forceinline__ bool key_is_nan(uint32_t k) { return KeyTraits<float>::key_is_nan(k); }
+  static __device__ __forceinline__ bool is_zero_key(uint32_t k) { return k == 0x80000000u; }
+  static __device__ __forceinline__ __nv_bfloat16 from_key(uint32_t k) {
+    return __float2bfloat16_rn(KeyTraits<float>::from_key(k));  // exact: the key came from a bf16
+  }
 };
 template <> struct KeyTraits<int32_t> {
   using K = uint32_t;
   static __device__ __forceinline__ K key(int32_t x) { return (uint32_t)x ^ 0x80000000u; }
   static __device__ __forceinline__ bool isnan_(int32_t) { return false; }
+  static constexpr bool kHasNan = false;
+  static __device__ __forceinline__ bool key_is_nan(uint32_t) { return false; }
+  static __device__ __forceinline__ bool is_zero_key(uint32_t) { return false; }
+  static __device__ __forceinline__ int32_t from_key(uint32_t k) { return (int32_t)(k ^ 0x80000000u); }
 };
 template <> struct KeyTraits<int64_t> {
   using K = uint64_t;
@@ -73,68 +102,102 @@ template <typename K> struct Digits {
 
 
 // ---------------------------------------------------------------------------
-// row groups of RG warps (N <= 2048): keys in registers, one radix pass,
+// row groups of RG warps (N <= 512 * RG): keys in registers, one radix pass,
 // compaction of the selected bucket, selection on the compacted list
 // ---------------------------------------------------------------------------
-// Element e of a row is held by warp w of the group, lane `lane`, slot (i, c):
-//   e = ((i * RG + w) * 32 + lane) * VW + c
-// (16-byte vectors when VW > 1).  The list holds composites
-//   (key << 32) | index
-// whose ascending order is the stable sort order, so the k-th composite is the
-// answer without a separate tie rule.
+// Each thread holds 16 elements of the row.  Element e is held by warp w of the
+// group, lane `lane`, slot (i, c):
+//   e = ((i * RG + w) * 32 + lane) * VW + c          (16-byte vectors when VW > 1)
+// The row group has kCap = 512 * RG slots; the first pass histograms the top
+// kDig = log2(kCap) key bits into kCap bins (16 bins per thread).  The bucket's
+// elements are compacted as 32-bit composites
+//   (key << kDig) | e
+// (the bucket's kDig key bits shift out, the index fills the freed bits), whose
+// ascending order is the stable sort order of the bucket.
 template <int RG>
 __device__ __forceinline__ void group_sync(int g) {
   if (RG == 1) __syncwarp();
   else asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(RG * 32) : "memory");
 }
 
-// Per-row-group scratch: CAP = elements per row group (list capacity), HW =
-// histogram words (bins / 2, packed 16-bit counters).
-// The histogram comes first and the struct is 16-byte aligned: the histogram
-// is cleared with 16-byte stores (HW is a multiple of 4).
-template <int RG, int CAP, int HW>
-struct __align__(16) GroupSmem {
-  static_assert(HW % 4 == 0, "histogram words must be a multiple of 4");
-  uint32_t hist[HW];
-  unsigned long long list[CAP];
-  unsigned long long first_nan;
-  uint32_t wsum[RG];
-  uint32_t bucket, below, count, ncand;
+template <int RG>
+struct RowGeom {
+  static constexpr int kThreads = RG * 32;
+  static constexpr int kCap = 16 * kThreads;
+  static constexpr int kDig = RG == 1 ? 9 : (RG == 2 ? 10 : 11);
+  static constexpr int kSh = 32 - kDig;
+  static_assert((1 << kDig) == kCap, "one bin per slot");
 };
 
-// Finds the bin holding rank r among nbins bins (packed pairs in hist).
-// Returns (bin, #elements in lower bins, #elements in bin) to every thread.
-template <int RG, class GS>
-__device__ __forceinline__ void group_find(GS& S, int g, int nbins, uint32_t r,
-                                           uint32_t& bin, uint32_t& below, uint32_t& cnt) {
-  const int t = threadIdx.x & (RG * 32 - 1);
-  const int lane = t & 31, w = t >> 5;
-  const int per = (nbins >> 1) / (RG * 32);  // words per thread (>= 1)
-  const uint32_t* hw = S.hist + t * per;
+template <int RG>
+struct __align__(16) RowSmem {
+  uint32_t hist[RowGeom<RG>::kCap];
+  uint32_t list[RowGeom<RG>::kCap];
+  uint32_t wsum[4];
+  uint32_t bucket, below, count, ncand;
+  uint32_t first_nan, pad[3];
+};
+
+// Every thread owns 16 consecutive bins: it reads them, zeroes them for the
+// next pass (no other thread reads them in this pass), and the group scans the
+// counts.  Returns to every thread the bin holding rank r, the count below it
+// and its count.  With `edge`, `special` reports a nonzero count in the first or
+// last 4 bins (where NaN and infinite float keys fall); the flag rides in bits
+// 20+ of the scanned words, above any count (counts <= 2048).
+template <int RG>
+__device__ __forceinline__ void row_find(RowSmem<RG>& S, int g, uint32_t r, bool edge,
+                                         uint32_t& bin, uint32_t& below, uint32_t& cnt,
+                                         bool& special) {
+  const int t = threadIdx.x & (RG * 32 - 1), lane = t & 31, w = t >> 5;
+  uint4* hp = reinterpret_cast<uint4*>(S.hist + 16 * t);
+  uint4 h[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = hp[j];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) hp[j] = make_uint4(0, 0, 0, 0);
+  const uint32_t c[16] = {h[0].x, h[0].y, h[0].z, h[0].w, h[1].x, h[1].y, h[1].z, h[1].w,
+                          h[2].x, h[2].y, h[2].z, h[2].w, h[3].x, h[3].y, h[3].z, h[3].w};
   uint32_t tot = 0;
-  for (int j = 0; j < per; ++j) tot += (hw[j] & 0xffffu) + (hw[j] >> 16);
-  uint32_t inc = tot;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) tot += c[j];
+  uint32_t sp = 0;
+  if (edge) {
+    if (t == 0) sp = (c[0] | c[1] | c[2] | c[3]) != 0u;
+    if (t == RG * 32 - 1) sp |= (c[12] | c[13] | c[14] | c[15]) != 0u;
+  }
+  uint32_t v = tot + (sp << 20);
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t x = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += x;
+    const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += y;
   }
   if (RG > 1) {
-    if (lane == 31) S.wsum[w] = inc;
+    if (lane == 31) S.wsum[w] = v;
     group_sync<RG>(g);
-    uint32_t off = 0;
-    for (int q = 0; q < w; ++q) off += S.wsum[q];
-    inc += off;
+    uint32_t off = 0, all = 0;
+#pragma unroll
+    for (int q = 0; q < RG; ++q) {
+      const uint32_t s = S.wsum[q];
+      off += (q < w) ? s : 0u;
+      all += s;
+    }
+    v += off;
+    special = (all >> 20) != 0u;
+  } else {
+    special = (__shfl_sync(0xffffffffu, v, 31) >> 20) != 0u;
   }
-  const uint32_t exc = inc - tot;
+  const uint32_t inc = v & 0xfffffu, exc = inc - tot;
   if (exc <= r && r < inc) {
     uint32_t acc = exc;
-    for (int j = 0; j < per; ++j) {
-      const uint32_t q = hw[j], c0 = q & 0xffffu, c1 = q >> 16;
-      if (r < acc + c0) { S.bucket = 2 * (t * per + j); S.below = acc; S.count = c0; break; }
-      acc += c0;
-      if (r < acc + c1) { S.bucket = 2 * (t * per + j) + 1; S.below = acc; S.count = c1; break; }
-      acc += c1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (r < acc + c[j]) {
+        S.bucket = 16 * t + j;
+        S.below = acc;
+        S.count = c[j];
+        break;
+      }
+      acc += c[j];
     }
   }
   group_sync<RG>(g);
@@ -143,210 +206,163 @@ __device__ __forceinline__ void group_find(GS& S, int g, int nbins, uint32_t r,
   cnt = S.count;
 }
 
-template <int RG, class GS>
-__device__ __forceinline__ void group_clear_hist(GS& S, int nbins) {
-  const int t = threadIdx.x & (RG * 32 - 1);
-  for (int j = t * 4; j < (nbins >> 1); j += RG * 32 * 4)
-    *reinterpret_cast<uint4*>(S.hist + j) = make_uint4(0, 0, 0, 0);
-}
-
-__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t d) {
-  atomicAdd(hist + (d >> 1), 1u << ((d & 1u) << 4));
-}
-
-template <int RG, int NI, int VW, int DIG0, int DIGL>
-using GroupSmemOf = GroupSmem<RG, RG * 32 * NI * VW, (1 << (DIG0 > DIGL ? DIG0 : DIGL)) / 2>;
-
-template <typename T, int RG, int NI, int VW, int DIG0, int DIGL, int GPC>
-__global__ void __launch_bounds__(GPC * RG * 32, 3)
-median_group_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restrict__ idxs,
-                    int64_t M, int N) {
+template <typename T, int RG, int VW, bool FULL, int GPC>
+__global__ void __launch_bounds__(GPC * RG * 32, 4)
+median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restrict__ idxs,
+                   int64_t M, int N) {
   using Tr = KeyTraits<T>;
-  using GS = GroupSmemOf<RG, NI, VW, DIG0, DIGL>;
+  using G = RowGeom<RG>;
   static_assert(sizeof(typename Tr::K) == 4, "32-bit keys only");
+  constexpr int NI = 16 / VW;
+  constexpr int kSh = G::kSh, kDig = G::kDig;
   extern __shared__ __align__(16) uint8_t median_smem[];
   const int g = threadIdx.x / (RG * 32);
   const int t = threadIdx.x & (RG * 32 - 1);
   const int lane = t & 31, w = t >> 5;
-  GS& S = reinterpret_cast<GS*>(median_smem)[g];
-  const int k = (N - 1) / 2;
-  constexpr int SH0 = 32 - DIG0;
+  RowSmem<RG>& S = reinterpret_cast<RowSmem<RG>*>(median_smem)[g];
+  const uint32_t k = (uint32_t)(N - 1) / 2;
 
-  // The next row's raw data is loaded into registers while the current row is
-  // selected (rows are ~8 KiB; the load latency is otherwise exposed per row).
-  constexpr int RN = VW > 1 ? 1 : VW;
-  uint4 rv[NI];           // 16-byte vectors (VW > 1)
-  T rs[NI][RN];           // scalars (VW == 1)
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    reinterpret_cast<uint4*>(S.hist + 16 * t)[j] = make_uint4(0, 0, 0, 0);
+  if (t == 0) {
+    S.ncand = 0;
+    S.first_nan = ~0u;
+  }
+  group_sync<RG>(g);
+
+  // The next row is loaded into registers while the current row is selected.
+  constexpr int RV = VW > 1 ? NI : 1;
+  constexpr int RS = VW > 1 ? 1 : 16;
+  uint4 rv[RV];
+  T rs[RS];
   auto load_row = [&](int64_t rrow) {
     if (rrow >= M) return;
     const T* xx = x + rrow * (int64_t)N;
+    if constexpr (VW > 1) {
 #pragma unroll
-    for (int i = 0; i < NI; ++i) {
-      const int base = ((i * RG + w) * 32 + lane) * VW;
-      if (VW > 1) {
-        rv[i] = (base + VW <= N) ? ld_global_stream_v4(xx + base) : make_uint4(0, 0, 0, 0);
-      } else {
+      for (int i = 0; i < NI; ++i) {
+        const int base = ((i * RG + w) * 32 + lane) * VW;
+        rv[i] = (FULL || base < N) ? ld_global_stream_v4(xx + base) : make_uint4(0, 0, 0, 0);
+      }
+    } else {
 #pragma unroll
-        for (int c = 0; c < RN; ++c) rs[i][c] = (base + c < N) ? xx[base + c] : T(0);
+      for (int i = 0; i < 16; ++i) {
+        const int e = (i * RG + w) * 32 + lane;
+        rs[i] = (FULL || e < N) ? xx[e] : T(0);
       }
     }
   };
+  auto elem = [&](int i, int c) { return ((i * RG + w) * 32 + lane) * VW + c; };
+
   const int64_t row0 = (int64_t)blockIdx.x * GPC + g;
   const int64_t rstep = (int64_t)gridDim.x * GPC;
   load_row(row0);
 
   for (int64_t row = row0; row < M; row += rstep) {
-    const T* xr = x + row * (int64_t)N;
-    uint32_t key[NI][VW];
-    bool nan_seen = false;
+    uint32_t key[16];
 #pragma unroll
-    for (int i = 0; i < NI; ++i) {
-      const int base = ((i * RG + w) * 32 + lane) * VW;
-      if (VW > 1) {
-        const T* e = reinterpret_cast<const T*>(&rv[i]);
+    for (int i = 0; i < NI; ++i)
 #pragma unroll
-        for (int c = 0; c < VW; ++c) {
-          key[i][c] = Tr::key(e[c]);
-          nan_seen |= (base + c < N) && Tr::isnan_(e[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < VW; ++c) {
-          const T vv = rs[i][c < RN ? c : 0];
-          key[i][c] = (base + c < N) ? Tr::key(vv) : 0u;
-          nan_seen |= (base + c < N) && Tr::isnan_(vv);
-        }
+      for (int c = 0; c < VW; ++c) {
+        if constexpr (VW > 1) key[i * VW + c] = Tr::key(reinterpret_cast<const T*>(&rv[i])[c]);
+        else key[i] = Tr::key(rs[i]);
       }
-    }
     load_row(row + rstep);
-    if (t == 0) {
-      S.first_nan = ~0ull;
-      S.ncand = 0;
-    }
-    group_clear_hist<RG>(S, 1 << DIG0);
-    group_sync<RG>(g);
 
-    // ---- NaN: the first NaN in index order decides the row
-    const bool any_nan = (RG == 1) ? __any_sync(0xffffffffu, nan_seen) : false;
-    if (RG > 1 && nan_seen) atomicMin(&S.first_nan, 0ull);  // flag; resolved below
-    if (RG > 1) group_sync<RG>(g);
-    if ((RG == 1 && any_nan) || (RG > 1 && S.first_nan == 0ull)) {
-      if (RG > 1) {
-        group_sync<RG>(g);
-        if (t == 0) S.first_nan = ~0ull;
-        group_sync<RG>(g);
-      }
-      unsigned long long mine = ~0ull;
+    // ---- pass 0 over registers: top kDig bits
+#pragma unroll
+    for (int i = 0; i < NI; ++i)
+#pragma unroll
+      for (int c = 0; c < VW; ++c)
+        if (FULL || elem(i, c) < N) atomicAdd(S.hist + (key[i * VW + c] >> kSh), 1u);
+    group_sync<RG>(g);
+    uint32_t b0, below, cnt;
+    bool special;
+    row_find<RG>(S, g, k, Tr::kHasNan, b0, below, cnt, special);
+
+    if (Tr::kHasNan && special) {
+      // a NaN or an infinity is present: the first NaN (in index order) decides
+      uint32_t mine = ~0u;
 #pragma unroll
       for (int i = 0; i < NI; ++i)
 #pragma unroll
         for (int c = 0; c < VW; ++c) {
-          const int e = ((i * RG + w) * 32 + lane) * VW + c;
-          if (e < N && Tr::isnan_(xr[e]) && (unsigned long long)e < mine) mine = e;
+          const uint32_t e = (uint32_t)elem(i, c);
+          if ((FULL || (int)e < N) && Tr::key_is_nan(key[i * VW + c]) && e < mine) mine = e;
         }
-      if (RG == 1) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const unsigned long long other = __shfl_xor_sync(0xffffffffu, mine, o);
-          mine = other < mine ? other : mine;
+      if (mine != ~0u) atomicMin(&S.first_nan, mine);
+      group_sync<RG>(g);
+      const uint32_t fn = S.first_nan;
+      group_sync<RG>(g);
+      if (fn != ~0u) {
+        if (t == 0) {
+          idxs[row] = (int64_t)fn;
+          vals[row] = x[row * (int64_t)N + fn];
+          S.first_nan = ~0u;
         }
-        if (lane == 0) S.first_nan = mine;
-      } else if (mine != ~0ull) {
-        atomicMin(&S.first_nan, mine);
+        continue;
       }
-      group_sync<RG>(g);
-      if (t == 0) {
-        idxs[row] = (int64_t)S.first_nan;
-        vals[row] = xr[S.first_nan];
-      }
-      group_sync<RG>(g);
-      continue;
     }
+    uint32_t r = k - below;
 
-    // ---- pass 0 over registers: top DIG0 bits
+    // ---- compact the bucket's elements as (key << kDig) | index
+    const uint32_t lo = b0 << kSh;
 #pragma unroll
     for (int i = 0; i < NI; ++i)
 #pragma unroll
       for (int c = 0; c < VW; ++c) {
-        const int e = ((i * RG + w) * 32 + lane) * VW + c;
-        if (e < N) hist_add(S.hist, key[i][c] >> SH0);
-      }
-    group_sync<RG>(g);
-    uint32_t b0, below, cnt;
-    group_find<RG>(S, g, 1 << DIG0, (uint32_t)k, b0, below, cnt);
-    uint32_t r = (uint32_t)k - below;
-
-    // ---- compact the bucket's elements as (key << 32 | index)
-#pragma unroll
-    for (int i = 0; i < NI; ++i)
-#pragma unroll
-      for (int c = 0; c < VW; ++c) {
-        const int e = ((i * RG + w) * 32 + lane) * VW + c;
-        if (e < N && (key[i][c] >> SH0) == b0) {
+        const uint32_t kk = key[i * VW + c];
+        if ((FULL || elem(i, c) < N) && (kk - lo) < (1u << kSh)) {
           const uint32_t pos = atomicAdd(&S.ncand, 1u);
-          S.list[pos] = ((unsigned long long)key[i][c] << 32) | (uint32_t)e;
+          S.list[pos] = (kk << kDig) | (uint32_t)elem(i, c);
         }
       }
     group_sync<RG>(g);
-    const uint32_t C = cnt;  // == S.ncand
-    unsigned long long ans = 0;
-    if (C <= 32) {
-      // one warp: bitonic sort of <= 32 composites, pick the r-th
+
+    uint32_t comp = 0;
+    bool owner = false;
+    if (cnt <= 32) {
+      // one warp: the composite with exactly r smaller composites
       if (w == 0) {
-        unsigned long long v = lane < (int)C ? S.list[lane] : ~0ull;
-#pragma unroll
-        for (int kk = 2; kk <= 32; kk <<= 1) {
-#pragma unroll
-          for (int j = kk >> 1; j > 0; j >>= 1) {
-            const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, j);
-            const bool up = ((lane & kk) == 0);
-            const bool lower = ((lane & j) == 0);
-            const unsigned long long mn = o < v ? o : v, mx = o < v ? v : o;
-            v = (lower == up) ? mn : mx;
-          }
-        }
-        ans = __shfl_sync(0xffffffffu, v, r);
-        if (lane == 0) S.list[0] = ans;  // publish (list no longer needed)
+        const uint32_t v = (uint32_t)lane < cnt ? S.list[lane] : ~0u;
+        uint32_t rank = 0;
+        for (uint32_t j = 0; j < cnt; ++j) rank += S.list[j] < v ? 1u : 0u;
+        owner = (uint32_t)lane < cnt && rank == r;
+        comp = v;
+        __syncwarp();
+        if (lane == 0) S.ncand = 0;
       }
-      group_sync<RG>(g);
-      ans = S.list[0];
     } else {
-      // radix passes over the list: remaining key bits, then the index bits
-      // composite digit source: c = (key << 32) | idx; key bits [SH0-1 .. 0], idx bits [10..0]
-      unsigned long long pref = 0, pmask = 0;
-      const int nb_key = SH0;  // remaining key bits
-      // pass plan over a virtual (nb_key + 11)-bit value v = (key & lowmask) << 11 | idx
-      const int tot_bits = nb_key + 11;
-      for (int done = 0; done < tot_bits;) {
-        const int wbits = (tot_bits - done) < DIGL ? (tot_bits - done) : DIGL;
-        const int sh = tot_bits - done - wbits;
-        group_sync<RG>(g);
-        group_clear_hist<RG>(S, 1 << DIGL);
-        group_sync<RG>(g);
-        for (uint32_t q = t; q < C; q += RG * 32) {
-          const unsigned long long cpx = S.list[q];
-          const unsigned long long vv =
-              ((cpx >> 32) & ((1ull << nb_key) - 1ull)) << 11 | (cpx & 0x7ffull);
-          if ((vv & pmask) == pref) hist_add(S.hist, (uint32_t)(vv >> sh) & ((1u << wbits) - 1u));
+      // radix passes over the list, kDig bits at a time from the top
+      uint32_t pref = 0;
+#pragma unroll 1
+      for (int done = 0; done < 32;) {
+        const int wb = (32 - done) < kDig ? (32 - done) : kDig;
+        const int sh = 32 - done - wb;
+        const uint32_t hmask = done == 0 ? 0u : (~0u << (32 - done));
+        for (uint32_t q = t; q < cnt; q += RG * 32) {
+          const uint32_t cq = S.list[q];
+          if ((cq & hmask) == pref) atomicAdd(S.hist + ((cq >> sh) & ((1u << wb) - 1u)), 1u);
         }
         group_sync<RG>(g);
         uint32_t bb, bl, bc;
-        group_find<RG>(S, g, 1 << DIGL, r, bb, bl, bc);
+        bool dummy;
+        row_find<RG>(S, g, r, false, bb, bl, bc, dummy);
         r -= bl;
-        pref |= (unsigned long long)bb << sh;
-        pmask |= (unsigned long long)((1u << wbits) - 1u) << sh;
-        done += wbits;
+        pref |= bb << sh;
+        done += wb;
       }
-      // pref now holds (remaining key bits, index)
-      ans = ((unsigned long long)b0 << (32 + SH0)) | ((pref >> 11) << 32) | (pref & 0x7ffull);
+      comp = pref;
+      owner = (t == 0);
+      if (t == 0) S.ncand = 0;
     }
-    if (t == 0) {
-      int64_t e = (int64_t)(uint32_t)ans;
-      if (e >= N) e = 0;  // unreachable; keeps the read in bounds
-      idxs[row] = e;
-      vals[row] = xr[e];
+    if (owner) {
+      const uint32_t e = comp & ((1u << kDig) - 1u);
+      const uint32_t kf = lo | (comp >> kDig);
+      idxs[row] = (int64_t)e;
+      vals[row] = Tr::is_zero_key(kf) ? x[row * (int64_t)N + e] : Tr::from_key(kf);
     }
-    group_sync<RG>(g);
   }
 }
 
@@ -478,12 +494,11 @@ median_cta_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __rest
 // ---------------------------------------------------------------------------
 // dispatch
 // ---------------------------------------------------------------------------
-template <typename T, int RG, int NI, int VW, int DIG0>
-int launch_group(const void* x, void* v, int64_t* idx, int64_t M, int N, cudaStream_t st) {
-  constexpr int GPC = 8 / RG;                 // groups per CTA (256 threads)
-  constexpr int DIGL = RG == 1 ? 8 : 11;      // digit width of the list passes
-  auto kern = median_group_kernel<T, RG, NI, VW, DIG0, DIGL, GPC>;
-  const int smem = (int)(GPC * sizeof(GroupSmemOf<RG, NI, VW, DIG0, DIGL>));
+template <typename T, int RG, int VW, bool FULL>
+int launch_rows(const void* x, void* v, int64_t* idx, int64_t M, int N, cudaStream_t st) {
+  constexpr int GPC = 8 / RG;  // row groups per CTA (256 threads)
+  auto kern = median_rows_kernel<T, RG, VW, FULL, GPC>;
+  const int smem = (int)(GPC * sizeof(RowSmem<RG>));
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
     set_error("median: cannot reserve %d bytes of shared memory", smem);
@@ -496,24 +511,30 @@ int launch_group(const void* x, void* v, int64_t* idx, int64_t M, int N, cudaStr
   int64_t grid = (int64_t)num_sms() * per_sm;
   if (grid > need) grid = need;
   kern<<<(unsigned)grid, GPC * RG * 32, smem, st>>>((const T*)x, (T*)v, idx, M, N);
-  return check_launch("median_group_kernel");
+  return check_launch("median_rows_kernel");
 }
 
-// Row length -> group width RG (warps), slots NI per lane, vector width VW.
+template <typename T, int RG, int VW>
+int launch_rows_n(const void* x, void* v, int64_t* idx, int64_t M, int N, cudaStream_t st) {
+  if constexpr (VW > 1) {
+    if (N == RowGeom<RG>::kCap) return launch_rows<T, RG, VW, true>(x, v, idx, M, N, st);
+  }
+  return launch_rows<T, RG, VW, false>(x, v, idx, M, N, st);
+}
+
+// Row length -> group width RG (warps); 16 elements per thread.
 template <typename T>
-int dispatch_group(const void* x, void* v, int64_t* idx, int64_t M, int N, bool vec,
-                   cudaStream_t st) {
+int dispatch_rows(const void* x, void* v, int64_t* idx, int64_t M, int N, bool vec,
+                  cudaStream_t st) {
   constexpr int VWV = 16 / sizeof(T);
   if (vec) {
-    // 16-byte vectors: 32 * RG * NI * VWV >= N
-    if (N <= 32 * VWV * 4) return launch_group<T, 1, 4, VWV, 8>(x, v, idx, M, N, st);
-    if (N <= 64 * VWV * 4) return launch_group<T, 2, 4, VWV, 11>(x, v, idx, M, N, st);
-    return launch_group<T, 4, 4, VWV, 11>(x, v, idx, M, N, st);
+    if (N <= 512) return launch_rows_n<T, 1, VWV>(x, v, idx, M, N, st);
+    if (N <= 1024) return launch_rows_n<T, 2, VWV>(x, v, idx, M, N, st);
+    return launch_rows_n<T, 4, VWV>(x, v, idx, M, N, st);
   }
-  if (N <= 256) return launch_group<T, 1, 8, 1, 8>(x, v, idx, M, N, st);
-  if (N <= 512) return launch_group<T, 1, 16, 1, 8>(x, v, idx, M, N, st);
-  if (N <= 1024) return launch_group<T, 2, 16, 1, 11>(x, v, idx, M, N, st);
-  return launch_group<T, 4, 16, 1, 11>(x, v, idx, M, N, st);
+  if (N <= 512) return launch_rows_n<T, 1, 1>(x, v, idx, M, N, st);
+  if (N <= 1024) return launch_rows_n<T, 2, 1>(x, v, idx, M, N, st);
+  return launch_rows_n<T, 4, 1>(x, v, idx, M, N, st);
 }
 
 template <typename T>
@@ -529,7 +550,7 @@ int median_dim_t(const void* x, void* v, int64_t* idx, int64_t M, int64_t N, cud
   if (sizeof(T) <= 4 && N <= 2048) {
     constexpr int VWV = 16 / (sizeof(T) <= 4 ? sizeof(T) : 4);
     const bool vec = aligned16(x) && ((N * (int64_t)sizeof(T)) % 16 == 0) && N >= 32 * VWV;
-    return dispatch_group<T>(x, v, idx, M, (int)N, vec, st);
+    return dispatch_rows<T>(x, v, idx, M, (int)N, vec, st);
   }
   return launch_cta<T>(x, v, idx, M, N, st);
 }

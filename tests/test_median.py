@@ -131,3 +131,41 @@ def test_deterministic():
     x = torch.randint(-5, 5, (512, 999)).float().to(DEV)
     a, b = median(x, dim=1), median(x, dim=1)
     assert torch.equal(a.indices, b.indices)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("N", [512, 1024, 2048])
+def test_special_values_full_rows(dtype, N):
+    """Rows that exactly fill a row group (the unpredicated kernel), with NaN,
+    infinities, signed zeros, all-equal rows and wide buckets (uniform data)."""
+    g = torch.Generator().manual_seed(N)
+    x = torch.randn(48, N, generator=g)
+    x[0] = 0.0
+    x[1, ::2] = -0.0
+    x[2, N - 1] = float("nan")
+    x[3, 7:] = float("nan")
+    x[4] = float("inf")
+    x[5, : N // 2 + 3] = float("-inf")
+    x[6, 9] = float("nan"); x[6, 4] = float("-nan")
+    x[7] = torch.where(torch.rand(N, generator=g) < 0.5, torch.tensor(-0.0), torch.tensor(0.0))
+    x[8] = 3.0
+    x[9, ::3] = float("inf")
+    x[10, 1::2] = float("-inf")
+    x[11:20] = torch.rand(9, N, generator=g)                 # ~N/8 keys per top-digit bucket
+    x[20:24] = torch.randint(-2, 3, (4, N), generator=g).float()
+    x[24] = torch.arange(N).float()
+    x[25] = -torch.arange(N).float()
+    x[26, N // 2:] = 1e-40                                  # subnormals
+    x[27] = torch.full((N,), -1e-40)
+    _exact(x.to(dtype))
+
+
+@pytest.mark.parametrize("N", [512, 2048])
+def test_int32_full_rows(N):
+    g = torch.Generator().manual_seed(1)
+    x = torch.randint(-2**31, 2**31 - 1, (40, N), generator=g, dtype=torch.int64).to(torch.int32)
+    x[0] = 7
+    x[1, ::2] = -2**31
+    x[2] = 2**31 - 1
+    x[3:10] = torch.randint(-3, 3, (7, N), generator=g).to(torch.int32)
+    _exact(x)
