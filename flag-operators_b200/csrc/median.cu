@@ -25,6 +25,7 @@
 // passes re-read the row (L2 hits for rows that fit in L2); after the last pass
 // the key of the k-th element is known and the answer is found with ballots.
 #include "common.cuh"
+#include "tc05.cuh"
 
 namespace fo {
 namespace {
@@ -114,6 +115,12 @@ template <typename K> struct Digits {
 //   (key << kDig) | e
 // (the bucket's kDig key bits shift out, the index fills the freed bits), whose
 // ascending order is the stable sort order of the bucket.
+//
+// The kernel is bound by the latency of its chain of shared-memory round trips
+// and group barriers per row, so the chain is kept short: warp totals come from
+// one redux, lane prefixes from bit-serial ballots (no shuffle chain), the
+// compaction appends to per-warp lists with ballots (no atomic round trip), and
+// the final selection reads all candidates with 16-byte loads.
 template <int RG>
 __device__ __forceinline__ void group_sync(int g) {
   if (RG == 1) __syncwarp();
@@ -129,30 +136,49 @@ struct RowGeom {
   static_assert((1 << kDig) == kCap, "one bin per slot");
 };
 
+// Bin b is stored at word hslot(b): bits 2-3 of b are XORed with bits 5-6, so
+// the 16-byte chunks the scan reads (chunk j of thread t = bins 16t + 4j ..)
+// land on distinct banks within every quarter warp (a 4-way conflict otherwise).
+__device__ __forceinline__ uint32_t hslot(uint32_t b) { return b ^ ((b >> 3) & 0xcu); }
+
+__device__ __forceinline__ uint32_t lanemask_le() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_le;" : "=r"(m));
+  return m;
+}
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
 template <int RG>
 struct __align__(16) RowSmem {
   uint32_t hist[RowGeom<RG>::kCap];
-  uint32_t list[RowGeom<RG>::kCap];
-  uint32_t wsum[4];
-  uint32_t bucket, below, count, ncand;
-  uint32_t first_nan, pad[3];
+  uint32_t list[RowGeom<RG>::kCap];  // RG per-warp regions of 512 composites
+  uint32_t tmp[32];                  // candidates of the final selection
+  uint32_t wsum[4];                  // per-warp totals (+ edge flags in bits 20+)
+  uint32_t wcnt[4];                  // per-warp candidate counts
+  uint32_t bucket, below, count, first_nan;
 };
 
 // Every thread owns 16 consecutive bins: it reads them, zeroes them for the
-// next pass (no other thread reads them in this pass), and the group scans the
-// counts.  Returns to every thread the bin holding rank r, the count below it
-// and its count.  With `edge`, `special` reports a nonzero count in the first or
-// last 4 bins (where NaN and infinite float keys fall); the flag rides in bits
-// 20+ of the scanned words, above any count (counts <= 2048).
+// next pass (no other thread reads them in this pass), and the group locates
+// the bin holding rank r.  Returns to every thread that bin, the count below it
+// and its count.  With `edge`, `special` reports a nonzero count in the first
+// or last 4 bins (where NaN and infinite float keys fall); the flag rides in
+// bits 20+ of the warp totals, above any count (counts <= 2048).
 template <int RG>
 __device__ __forceinline__ void row_find(RowSmem<RG>& S, int g, uint32_t r, bool edge,
                                          uint32_t& bin, uint32_t& below, uint32_t& cnt,
                                          bool& special) {
+  constexpr int kTotBits = RowGeom<RG>::kDig + 1;  // a thread's total is <= kCap
   const int t = threadIdx.x & (RG * 32 - 1), lane = t & 31, w = t >> 5;
   uint4* hp = reinterpret_cast<uint4*>(S.hist + 16 * t);
+  const int sw = (t >> 1) & 3;  // chunk j of this thread is stored at chunk j ^ sw
   uint4 h[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) h[j] = hp[j];
+  for (int j = 0; j < 4; ++j) h[j] = hp[j ^ sw];
 #pragma unroll
   for (int j = 0; j < 4; ++j) hp[j] = make_uint4(0, 0, 0, 0);
   const uint32_t c[16] = {h[0].x, h[0].y, h[0].z, h[0].w, h[1].x, h[1].y, h[1].z, h[1].w,
@@ -165,39 +191,48 @@ __device__ __forceinline__ void row_find(RowSmem<RG>& S, int g, uint32_t r, bool
     if (t == 0) sp = (c[0] | c[1] | c[2] | c[3]) != 0u;
     if (t == RG * 32 - 1) sp |= (c[12] | c[13] | c[14] | c[15]) != 0u;
   }
-  uint32_t v = tot + (sp << 20);
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += y;
-  }
+  const uint32_t wt = __reduce_add_sync(0xffffffffu, tot + (sp << 20));
+  uint32_t off = 0, all = wt;
+  int ow = 0;  // the warp whose bins hold rank r
   if (RG > 1) {
-    if (lane == 31) S.wsum[w] = v;
+    if (lane == 0) S.wsum[w] = wt;
     group_sync<RG>(g);
-    uint32_t off = 0, all = 0;
+    all = 0;
+    uint32_t cum = 0;
 #pragma unroll
     for (int q = 0; q < RG; ++q) {
       const uint32_t s = S.wsum[q];
-      off += (q < w) ? s : 0u;
       all += s;
-    }
-    v += off;
-    special = (all >> 20) != 0u;
-  } else {
-    special = (__shfl_sync(0xffffffffu, v, 31) >> 20) != 0u;
-  }
-  const uint32_t inc = v & 0xfffffu, exc = inc - tot;
-  if (exc <= r && r < inc) {
-    uint32_t acc = exc;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (r < acc + c[j]) {
-        S.bucket = 16 * t + j;
-        S.below = acc;
-        S.count = c[j];
-        break;
+      const uint32_t cq = s & 0xfffffu;
+      if (ow == q && r >= cum + cq && q + 1 < RG) {
+        cum += cq;
+        ow = q + 1;
       }
-      acc += c[j];
+    }
+    off = cum;
+  }
+  special = (all >> 20) != 0u;
+  if (w == ow) {
+    // lane prefixes of the owner warp from one ballot per bit of the totals
+    const uint32_t le = lanemask_le();
+    uint32_t inc = 0;
+#pragma unroll
+    for (int b = 0; b < kTotBits; ++b)
+      inc += (uint32_t)__popc(__ballot_sync(0xffffffffu, (tot >> b) & 1u) & le) << b;
+    inc += off;
+    const uint32_t exc = inc - tot;
+    if (exc <= r && r < inc) {
+      uint32_t acc = exc;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (r < acc + c[j]) {
+          S.bucket = 16 * t + j;
+          S.below = acc;
+          S.count = c[j];
+          break;
+        }
+        acc += c[j];
+      }
     }
   }
   group_sync<RG>(g);
@@ -206,8 +241,10 @@ __device__ __forceinline__ void row_find(RowSmem<RG>& S, int g, uint32_t r, bool
   cnt = S.count;
 }
 
+// 4 CTAs per SM (64 registers) for rows that fill the group; the predicated
+// variants need more registers.
 template <typename T, int RG, int VW, bool FULL, int GPC>
-__global__ void __launch_bounds__(GPC * RG * 32, 4)
+__global__ void __launch_bounds__(GPC * RG * 32, FULL ? 4 : 3)
 median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restrict__ idxs,
                    int64_t M, int N) {
   using Tr = KeyTraits<T>;
@@ -215,6 +252,7 @@ median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __res
   static_assert(sizeof(typename Tr::K) == 4, "32-bit keys only");
   constexpr int NI = 16 / VW;
   constexpr int kSh = G::kSh, kDig = G::kDig;
+  constexpr int kRegion = 512;  // list words per warp
   extern __shared__ __align__(16) uint8_t median_smem[];
   const int g = threadIdx.x / (RG * 32);
   const int t = threadIdx.x & (RG * 32 - 1);
@@ -225,10 +263,7 @@ median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __res
 #pragma unroll
   for (int j = 0; j < 4; ++j)
     reinterpret_cast<uint4*>(S.hist + 16 * t)[j] = make_uint4(0, 0, 0, 0);
-  if (t == 0) {
-    S.ncand = 0;
-    S.first_nan = ~0u;
-  }
+  if (t == 0) S.first_nan = ~0u;
   group_sync<RG>(g);
 
   // The next row is loaded into registers while the current row is selected.
@@ -259,7 +294,8 @@ median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __res
   const int64_t rstep = (int64_t)gridDim.x * GPC;
   load_row(row0);
 
-  for (int64_t row = row0; row < M; row += rstep) {
+  int fw = 0;  // the warp that finishes this row (rotates, so no warp lags)
+  for (int64_t row = row0; row < M; row += rstep, fw = (fw + 1) & (RG - 1)) {
     uint32_t key[16];
 #pragma unroll
     for (int i = 0; i < NI; ++i)
@@ -275,7 +311,7 @@ median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __res
     for (int i = 0; i < NI; ++i)
 #pragma unroll
       for (int c = 0; c < VW; ++c)
-        if (FULL || elem(i, c) < N) atomicAdd(S.hist + (key[i * VW + c] >> kSh), 1u);
+        if (FULL || elem(i, c) < N) atomicAdd(S.hist + hslot(key[i * VW + c] >> kSh), 1u);
     group_sync<RG>(g);
     uint32_t b0, below, cnt;
     bool special;
@@ -306,45 +342,70 @@ median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __res
     }
     uint32_t r = k - below;
 
-    // ---- compact the bucket's elements as (key << kDig) | index
+    // ---- compact the bucket's elements as (key << kDig) | index, per warp
     const uint32_t lo = b0 << kSh;
+    {
+      uint32_t* L = S.list + kRegion * w;
+      const uint32_t lt = lanemask_lt();
+      uint32_t nw = 0;
 #pragma unroll
-    for (int i = 0; i < NI; ++i)
+      for (int i = 0; i < NI; ++i)
 #pragma unroll
-      for (int c = 0; c < VW; ++c) {
-        const uint32_t kk = key[i * VW + c];
-        if ((FULL || elem(i, c) < N) && (kk - lo) < (1u << kSh)) {
-          const uint32_t pos = atomicAdd(&S.ncand, 1u);
-          S.list[pos] = (kk << kDig) | (uint32_t)elem(i, c);
+        for (int c = 0; c < VW; ++c) {
+          const uint32_t kk = key[i * VW + c];
+          const bool m = (FULL || elem(i, c) < N) && (kk - lo) < (1u << kSh);
+          const uint32_t bal = __ballot_sync(0xffffffffu, m);
+          if (bal) {
+            if (m) L[nw + __popc(bal & lt)] = (kk << kDig) | (uint32_t)elem(i, c);
+            nw += __popc(bal);
+          }
         }
-      }
+      if (lane == 0) S.wcnt[w] = nw;
+    }
     group_sync<RG>(g);
 
     uint32_t comp = 0;
     bool owner = false;
     if (cnt <= 32) {
       // one warp: the composite with exactly r smaller composites
-      if (w == 0) {
-        const uint32_t v = (uint32_t)lane < cnt ? S.list[lane] : ~0u;
+      if (w == fw) {
+        uint32_t base = 0, v = ~0u;
+#pragma unroll
+        for (int q = 0; q < RG; ++q) {
+          const uint32_t nq = S.wcnt[q];
+          if ((uint32_t)lane >= base && (uint32_t)lane < base + nq)
+            v = S.list[kRegion * q + (lane - base)];
+          base += nq;
+        }
+        S.tmp[lane] = v;
+        __syncwarp();
         uint32_t rank = 0;
-        for (uint32_t j = 0; j < cnt; ++j) rank += S.list[j] < v ? 1u : 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 o = reinterpret_cast<const uint4*>(S.tmp)[j];
+          rank += (o.x < v) + (o.y < v) + (o.z < v) + (o.w < v);
+        }
         owner = (uint32_t)lane < cnt && rank == r;
         comp = v;
         __syncwarp();
-        if (lane == 0) S.ncand = 0;
       }
     } else {
-      // radix passes over the list, kDig bits at a time from the top
+      // radix passes over the per-warp lists, kDig bits at a time from the top
       uint32_t pref = 0;
+      uint32_t nq[RG];
+#pragma unroll
+      for (int q = 0; q < RG; ++q) nq[q] = S.wcnt[q];
 #pragma unroll 1
       for (int done = 0; done < 32;) {
         const int wb = (32 - done) < kDig ? (32 - done) : kDig;
         const int sh = 32 - done - wb;
         const uint32_t hmask = done == 0 ? 0u : (~0u << (32 - done));
-        for (uint32_t q = t; q < cnt; q += RG * 32) {
-          const uint32_t cq = S.list[q];
-          if ((cq & hmask) == pref) atomicAdd(S.hist + ((cq >> sh) & ((1u << wb) - 1u)), 1u);
-        }
+#pragma unroll
+        for (int q = 0; q < RG; ++q)
+          for (uint32_t u = t; u < nq[q]; u += RG * 32) {
+            const uint32_t cq = S.list[kRegion * q + u];
+            if ((cq & hmask) == pref) atomicAdd(S.hist + hslot((cq >> sh) & ((1u << wb) - 1u)), 1u);
+          }
         group_sync<RG>(g);
         uint32_t bb, bl, bc;
         bool dummy;
@@ -355,7 +416,6 @@ median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __res
       }
       comp = pref;
       owner = (t == 0);
-      if (t == 0) S.ncand = 0;
     }
     if (owner) {
       const uint32_t e = comp & ((1u << kDig) - 1u);
@@ -364,6 +424,365 @@ median_rows_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __res
       vals[row] = Tr::is_zero_key(kf) ? x[row * (int64_t)N + e] : Tr::from_key(kf);
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// rows of 1024 < N <= 2048 of 4-byte elements (16-byte aligned): producer and
+// consumer warps
+// ---------------------------------------------------------------------------
+// Two rates have to be met at once: HBM needs ~64 KiB of reads in flight per
+// SM at all times, and each row's selection is a chain of dependent
+// shared-memory round trips (scan, compaction, selection) several thousand
+// cycles long.  Warps that both load and select a row stall their loads for the
+// length of the chain, so the work is split (256 threads, 2 CTAs per SM):
+//   producers (4 warps): keep the next kWsPD rows in flight in registers (16
+//     elements per thread), turn the current row into keys, stage the keys and
+//     the row's 11-bit histogram in slot q % 4, and move on;
+//   consumers (4 warps, row q goes to consumer q % 4, which owns slot q % 4):
+//     scan the histogram (clearing it), compact the selected bucket from the
+//     staged keys, select, and hand the slot back.
+// Slots past the end of a shorter row hold the largest key (0xffffffff): they
+// sort after every element, so rank k is unchanged, and the NaN check allows
+// for them in the last bin.  Hand-offs are mbarriers, each waited on by one
+// role in phase order; waits are bounded (one that runs out sets the abort
+// flag, stops every role and is counted in g_median_timeouts).
+constexpr int kWsSlots = 4;   // = consumer warps
+constexpr int kWsPD = 4;      // rows in flight per producer thread
+constexpr int kWsCap = 2048;
+constexpr uint32_t kMedWaitLimit = 1u << 22;
+__device__ unsigned int g_median_timeouts;
+
+struct __align__(128) WsSmem {
+  uint32_t keys[kWsSlots][kWsCap];
+  uint32_t hist[kWsSlots][kWsCap];
+  unsigned long long list[kWsSlots][32];
+  uint32_t ccount[kWsSlots];
+  uint64_t full[kWsSlots], empty[kWsSlots];
+  uint32_t abort_flag;
+};
+
+// Bin b (consumer lane b / 64 owns 16 chunks of 4 bins) is stored at word
+// wsslot(b): the chunk index is XORed with the owner lane's low 3 bits, so the
+// consumer's 16-byte chunk reads hit distinct banks in every quarter warp.
+__device__ __forceinline__ uint32_t wsslot(uint32_t b) { return b ^ ((b >> 4) & 0x1cu); }
+
+__device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
+}
+
+// Bounded wait; false (with the abort flag set) when it runs out or when
+// another role has aborted.
+__device__ __forceinline__ bool ws_wait(WsSmem& S, uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMedWaitLimit; ++i) {
+    if (tc::mbar_try_wait(bar, parity)) return true;
+    if (*(volatile uint32_t*)&S.abort_flag) return false;
+  }
+  atomicAdd(&g_median_timeouts, 1u);
+  *(volatile uint32_t*)&S.abort_flag = 1;
+  return false;
+}
+
+// Consumer scan of a slot's 2048 bins (64 per lane): returns to every lane the
+// bin holding rank r, the count below it and its count, and zeroes the bins.
+// With `edge`, `special` reports a nonzero count in bins 0-3 or more than npad
+// in bins 2044-2047 (where NaN and infinite keys fall).
+__device__ __forceinline__ void ws_find(uint32_t* hist, uint32_t r, bool edge, uint32_t npad,
+                                        uint32_t& bin, uint32_t& below, uint32_t& cnt,
+                                        bool& special) {
+  const int lane = threadIdx.x & 31;
+  uint4* hp = reinterpret_cast<uint4*>(hist + 64 * lane);
+  const int sw = lane & 7;
+  uint32_t cs[16], tot = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint4 h = hp[j ^ sw];
+    cs[j] = h.x + h.y + h.z + h.w;
+    tot += cs[j];
+  }
+  bool sp = false;
+  if (edge) sp = (lane == 0 && cs[0] != 0u) || (lane == 31 && cs[15] != npad);
+  special = __any_sync(0xffffffffu, sp);
+  uint32_t inc = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  const uint32_t exc = inc - tot;
+  const bool own = exc <= r && r < inc;
+  const int ol = __ffs(__ballot_sync(0xffffffffu, own)) - 1;
+  uint32_t pb = 0, pbl = 0, pc = 0;
+  if (own) {
+    uint32_t acc = exc;
+    int jj = 0;
+#pragma unroll
+    for (int j = 0; j < 15; ++j)
+      if (jj == j && r >= acc + cs[j]) {
+        acc += cs[j];
+        jj = j + 1;
+      }
+    const uint4 q = hp[jj ^ sw];
+    const uint32_t c4[4] = {q.x, q.y, q.z, q.w};
+    int ww = 0;
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      if (ww == j && r >= acc + c4[j]) {
+        acc += c4[j];
+        ww = j + 1;
+      }
+    uint32_t cw = c4[0];
+#pragma unroll
+    for (int j = 1; j < 4; ++j)
+      if (ww == j) cw = c4[j];
+    pb = 64u * lane + 4u * jj + ww;
+    pbl = acc;
+    pc = cw;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) hp[j ^ sw] = make_uint4(0, 0, 0, 0);
+  bin = __shfl_sync(0xffffffffu, pb, ol);
+  below = __shfl_sync(0xffffffffu, pbl, ol);
+  cnt = __shfl_sync(0xffffffffu, pc, ol);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256, 2)
+median_ws_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restrict__ idxs,
+                 int64_t M, int N) {
+  using Tr = KeyTraits<T>;
+  static_assert(sizeof(T) == 4, "4-byte elements");
+  extern __shared__ __align__(128) uint8_t median_smem[];
+  WsSmem& S = *reinterpret_cast<WsSmem*>(median_smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t k = (uint32_t)(N - 1) / 2;
+  const uint32_t npad = (uint32_t)(kWsCap - N);
+  const int64_t rstep = gridDim.x;
+  // rows of this CTA: q-th row = blockIdx.x + q * gridDim.x
+  const int64_t nq = M > blockIdx.x ? (M - 1 - blockIdx.x) / rstep + 1 : 0;
+
+  for (int j = threadIdx.x; j < kWsSlots * kWsCap / 4; j += blockDim.x)
+    reinterpret_cast<uint4*>(&S.hist[0][0])[j] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x < kWsSlots) S.ccount[threadIdx.x] = 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWsSlots; ++s) {
+      tc::mbar_init(&S.full[s], 128);
+      tc::mbar_init(&S.empty[s], 32);
+    }
+    S.abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp < 4) {
+    // ---------------- producers
+    const int t = threadIdx.x;  // 0..127; element (i, c) = (i * 128 + t) * 4 + c
+    uint4 rv[kWsPD][4];
+    auto load_row = [&](int64_t q, uint4 (&dst)[4]) {
+      if (q >= nq) return;
+      const T* xx = x + (blockIdx.x + q * rstep) * (int64_t)N;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int base = (i * 128 + t) * 4;
+        dst[i] = base < N ? ld_global_stream_v4(xx + base) : make_uint4(0, 0, 0, 0);
+      }
+    };
+#pragma unroll
+    for (int j = 0; j < kWsPD; ++j) load_row(j, rv[j]);
+    bool stop = false;
+    for (int64_t qb = 0; qb < nq && !stop; qb += kWsPD) {
+#pragma unroll
+      for (int j = 0; j < kWsPD; ++j) {
+        // row qb + j lives in rv[j] and goes to slot j (kWsPD == kWsSlots)
+        const int64_t q = qb + j;
+        if (q >= nq || stop) break;
+        uint32_t key[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int base = (i * 128 + t) * 4;
+          const uint32_t vv[4] = {rv[j][i].x, rv[j][i].y, rv[j][i].z, rv[j][i].w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            key[4 * i + c] = base + c < N ? Tr::key(reinterpret_cast<const T*>(vv)[c]) : 0xffffffffu;
+        }
+        load_row(q + kWsPD, rv[j]);
+        const int64_t use = q / kWsSlots;
+        if (use > 0 && !ws_wait(S, &S.empty[j], (uint32_t)(use - 1) & 1u)) {
+          stop = true;
+          break;
+        }
+        uint32_t* K = S.keys[j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<uint4*>(K + (i * 128 + t) * 4) =
+              make_uint4(key[4 * i], key[4 * i + 1], key[4 * i + 2], key[4 * i + 3]);
+        uint32_t* H = S.hist[j];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) atomicAdd(H + wsslot(key[c] >> 21), 1u);
+        mbar_arrive1(&S.full[j]);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers
+  const int cw = warp - 4;
+  uint32_t* H = S.hist[cw];
+  unsigned long long* L = S.list[cw];
+  for (int64_t q = cw; q < nq; q += kWsSlots) {
+    const int64_t row = blockIdx.x + q * rstep;
+    if (!ws_wait(S, &S.full[cw], (uint32_t)(q / kWsSlots) & 1u)) break;
+    const uint32_t* K = S.keys[cw];
+    uint32_t b, below, cnt;
+    bool special;
+    ws_find(H, k, Tr::kHasNan, npad, b, below, cnt, special);
+    bool done = false;
+    if (Tr::kHasNan && special) {
+      // a NaN or an infinity is present: the first NaN (in index order) decides
+      uint32_t mine = ~0u;
+      for (int i = 0; i < 16; ++i) {
+        const int ch = i * 32 + lane;
+        const uint4 kv = reinterpret_cast<const uint4*>(K)[ch];
+        const uint32_t kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (4 * ch + c < N && Tr::key_is_nan(kk[c])) mine = min(mine, (uint32_t)(4 * ch + c));
+      }
+      const uint32_t fn = __reduce_min_sync(0xffffffffu, mine);
+      if (fn != ~0u) {
+        if (lane == 0) {
+          idxs[row] = (int64_t)fn;
+          vals[row] = x[row * (int64_t)N + fn];
+        }
+        done = true;
+      }
+    }
+    if (!done) {
+      uint32_t r = k - below;
+      uint32_t P = b << 21, Mk = 0xffe00000u;
+      int known = 11;
+      while (cnt > 32 && known < 32) {
+        // narrow the bucket with the next key bits (this warp's histogram)
+        const int nb = (32 - known) < 11 ? (32 - known) : 11;
+        const int sh = 32 - known - nb;
+        const uint32_t dm = (1u << nb) - 1u;
+        for (int i = 0; i < 16; ++i) {
+          const uint4 kv = reinterpret_cast<const uint4*>(K)[i * 32 + lane];
+          const uint32_t kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if ((kk[c] & Mk) == P) atomicAdd(H + wsslot((kk[c] >> sh) & dm), 1u);
+        }
+        __syncwarp();
+        uint32_t bb, bl;
+        bool unused;
+        ws_find(H, r, false, 0, bb, bl, cnt, unused);
+        r -= bl;
+        P |= bb << sh;
+        Mk |= dm << sh;
+        known += nb;
+      }
+      uint32_t e_ans = 0, k_ans = P;
+      bool owner = false;
+      if (cnt <= 32) {
+        // compact the bucket as (key << 32 | index): match masks first, then
+        // one slot reservation per lane that holds any
+        uint32_t mlo = 0, mhi = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint4 kv = reinterpret_cast<const uint4*>(K)[i * 32 + lane];
+          const uint32_t kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t bit = ((kk[c] & Mk) == P) ? 1u : 0u;
+            if (i < 8) mlo |= bit << (4 * i + c);
+            else mhi |= bit << (4 * (i - 8) + c);
+          }
+        }
+        const uint32_t nl = __popc(mlo) + __popc(mhi);
+        if (nl) {
+          uint32_t pos = atomicAdd(&S.ccount[cw], nl);
+          unsigned long long mm = ((unsigned long long)mhi << 32) | mlo;
+          while (mm) {
+            const int j = __ffsll((long long)mm) - 1;
+            mm &= mm - 1;
+            const uint32_t e = (uint32_t)(4 * ((j >> 2) * 32 + lane) + (j & 3));
+            L[pos++] = ((unsigned long long)K[e] << 32) | e;
+          }
+        }
+        __syncwarp();
+        const unsigned long long v = (uint32_t)lane < cnt ? L[lane] : ~0ull;
+        uint32_t rank = 0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const ulonglong2 o = reinterpret_cast<const ulonglong2*>(L)[j];
+          rank += ((uint32_t)(2 * j) < cnt && o.x < v) ? 1u : 0u;
+          rank += ((uint32_t)(2 * j + 1) < cnt && o.y < v) ? 1u : 0u;
+        }
+        owner = (uint32_t)lane < cnt && rank == r;
+        e_ans = (uint32_t)v;
+        k_ans = (uint32_t)(v >> 32);
+        if (lane == 0) S.ccount[cw] = 0;
+      } else {
+        // all key bits known: the r-th element equal to P in index order
+        for (int i = 0; i < 16; ++i) {
+          const int ch = i * 32 + lane;
+          const uint4 kv = reinterpret_cast<const uint4*>(K)[ch];
+          const uint32_t kk[4] = {kv.x, kv.y, kv.z, kv.w};
+          uint32_t mc = 0;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) mc += kk[c] == P ? 1u : 0u;
+          uint32_t inc = mc;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
+          }
+          const uint32_t total = __shfl_sync(0xffffffffu, inc, 31);
+          if (r < total) {
+            const uint32_t exc = inc - mc;
+            if (exc <= r && r < inc) {
+              uint32_t qq = r - exc;
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                if (kk[c] == P) {
+                  if (qq == 0 && !owner) {
+                    owner = true;
+                    e_ans = (uint32_t)(4 * ch + c);
+                  }
+                  --qq;
+                }
+            }
+            break;
+          }
+          r -= total;
+        }
+      }
+      if (owner) {
+        idxs[row] = (int64_t)e_ans;
+        vals[row] = Tr::is_zero_key(k_ans) ? x[row * (int64_t)N + e_ans] : Tr::from_key(k_ans);
+      }
+    }
+    __syncwarp();
+    mbar_arrive1(&S.empty[cw]);  // keys and the cleared histogram back to the producers
+  }
+}
+
+
+template <typename T>
+int launch_ws_rows(const void* x, void* v, int64_t* idx, int64_t M, int N, cudaStream_t st) {
+  auto kern = median_ws_kernel<T>;
+  const int smem = (int)sizeof(WsSmem);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+    set_error("median: cannot reserve %d bytes of shared memory", smem);
+    return FO_ECUDA;
+  }
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem);
+  if (per_sm < 1) per_sm = 1;
+  int64_t grid = (int64_t)num_sms() * per_sm;
+  if (grid > M) grid = M;
+  kern<<<(unsigned)grid, 256, smem, st>>>((const T*)x, (T*)v, idx, M, N);
+  return check_launch("median_ws_kernel");
 }
 
 // ---------------------------------------------------------------------------
@@ -384,7 +803,6 @@ median_cta_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __rest
   __shared__ uint32_t s_bucket, s_below;
   __shared__ int64_t s_found;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  constexpr int NW = kCtaThreads / 32;
   const int64_t k = (N - 1) / 2;
 
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
@@ -550,6 +968,9 @@ int median_dim_t(const void* x, void* v, int64_t* idx, int64_t M, int64_t N, cud
   if (sizeof(T) <= 4 && N <= 2048) {
     constexpr int VWV = 16 / (sizeof(T) <= 4 ? sizeof(T) : 4);
     const bool vec = aligned16(x) && ((N * (int64_t)sizeof(T)) % 16 == 0) && N >= 32 * VWV;
+    if constexpr (sizeof(T) == 4) {
+      if (vec && N > 1024) return launch_ws_rows<T>(x, v, idx, M, (int)N, st);
+    }
     return dispatch_rows<T>(x, v, idx, M, (int)N, vec, st);
   }
   return launch_cta<T>(x, v, idx, M, N, st);
