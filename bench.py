@@ -345,6 +345,8 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
             for red in ("sum", "prod", "amax", "amin", "mean"):
                 for inc in (True, False):
                     name = f"scatter_{dist_name}_{red}_{'self' if inc else 'noself'}"
+                    if not want(name):
+                        continue
                     ms = time_steps(lambda: scatter_reduce(sd, 0, idx_d, srd, red, include_self=inc),
                                     K, W, flush, dist)
                     cpu = None
@@ -357,14 +359,15 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
                     launches = 1 + (0 if (red in ("sum", "prod") and inc) else 2)
                     res[name] = hbm_entry(name, SCATTER_BYTES, ms, K, launches, hbm, src, traffic,
                                           cpu)
-        ms = time_steps(lambda: scatter_reduce(selfi_d, 0, iud, sid, "sum"), K, W, flush, dist)
-        cpu = None
-        if do_cpu:
-            si = torch.zeros(1 << 20, dtype=torch.int32)
-            cpu = cpu_entry(lambda: oracle.scatter_reduce(si, 0, idx_u[:sub], src_i[:sub], "sum"),
-                            sub * 12 + (1 << 20) * 8, "GB/s", "first 2^20 of 2^24 elements")
-        res["scatter_uniform_int32_sum"] = hbm_entry("scatter_uniform_int32_sum", SCATTER_BYTES, ms,
-                                                     K, 1, hbm, src, traffic, cpu)
+        if want("scatter_uniform_int32_sum"):
+            ms = time_steps(lambda: scatter_reduce(selfi_d, 0, iud, sid, "sum"), K, W, flush, dist)
+            cpu = None
+            if do_cpu:
+                si = torch.zeros(1 << 20, dtype=torch.int32)
+                cpu = cpu_entry(lambda: oracle.scatter_reduce(si, 0, idx_u[:sub], src_i[:sub], "sum"),
+                                sub * 12 + (1 << 20) * 8, "GB/s", "first 2^20 of 2^24 elements")
+            res["scatter_uniform_int32_sum"] = hbm_entry("scatter_uniform_int32_sum", SCATTER_BYTES,
+                                                         ms, K, 1, hbm, src, traffic, cpu)
         del sd, srd, iud, izd, sid, selfi_d
 
     # fused cross-entropy forward + backward

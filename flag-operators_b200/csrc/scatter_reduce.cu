@@ -21,6 +21,13 @@
 //  * Float amax/amin reduce order-preserving uint32 keys with native integer
 //    atomicMax/Min (no CAS loop); NaN maps to the extreme key so it wins.
 //    prod is the only CAS loop.
+//  * Float sum without self and float mean accumulate (sum, count) pairs in
+//    one interleaved scratch with a single 8-byte vector reduction
+//    (red.global.add.v2.f32) per update instead of two atomics; counts held
+//    as floats are exact while a call has at most 2^24 updates (else separate
+//    int32 counts).
+//  * The contiguous 1-D pass is software-pipelined: the next quad's index and
+//    src loads are in flight while the current quad's updates are issued.
 //  * A scratch accumulator (+ int32 counts) is used only when needed:
 //    include_self=False (to know which cells were reached), mean (counts),
 //    float amax/amin (keys) and 16-bit floats (fp32 accumulation).  Then an
@@ -109,6 +116,12 @@ __device__ __forceinline__ void atomic_min_a(int64_t* p, int64_t v) {
   atomicMin(reinterpret_cast<long long*>(p), (long long)v);
 }
 
+// (sum, count) pair update: one 8-byte vector reduction in L2
+__device__ __forceinline__ void red_pair(float* p, float v, float c) {
+  asm volatile("red.relaxed.gpu.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(v), "f"(c)
+               : "memory");
+}
+
 template <typename T> struct AccType { using A = T; };
 template <> struct AccType<__half> { using A = float; };
 template <> struct AccType<__nv_bfloat16> { using A = float; };
@@ -153,7 +166,8 @@ struct Geo {
   int ndim;
 };
 
-template <typename T, typename I, int OP, bool KEYS, bool CNT, int NDIM, bool VEC>
+// PAIR: acc holds interleaved (sum, count) floats and cnt is unused.
+template <typename T, typename I, int OP, bool KEYS, bool CNT, bool PAIR, int NDIM, bool VEC>
 __global__ void __launch_bounds__(kThreads)
 scatter_kernel(const T* __restrict__ src, const I* __restrict__ index,
                typename Acc<T, OP, KEYS>::A* __restrict__ acc, int32_t* __restrict__ cnt,
@@ -163,12 +177,13 @@ scatter_kernel(const T* __restrict__ src, const I* __restrict__ index,
   constexpr int kSlots = Slots<A>::kN;
   __shared__ uint32_t s_tag[kSlots];
   __shared__ A s_val[kSlots];
-  __shared__ int32_t s_cnt[CNT ? kSlots : 1];
+  constexpr bool kCnt = CNT || PAIR;
+  __shared__ int32_t s_cnt[kCnt ? kSlots : 1];
   if (use_cache) {
     for (int j = threadIdx.x; j < kSlots; j += blockDim.x) {
       s_tag[j] = kEmpty;
       s_val[j] = AT::identity();
-      if (CNT) s_cnt[j] = 0;
+      if (kCnt) s_cnt[j] = 0;
     }
     __syncthreads();
   }
@@ -185,40 +200,61 @@ scatter_kernel(const T* __restrict__ src, const I* __restrict__ index,
       }
       if (t == o32) {
         AT::op(&s_val[slot], v);
-        if (CNT) atomicAdd(&s_cnt[slot], 1);
+        if (kCnt) atomicAdd(&s_cnt[slot], 1);
         return;
       }
     }
-    AT::op(acc + off, v);
-    if (CNT) atomicAdd(cnt + off, 1);
+    if constexpr (PAIR) {
+      red_pair(reinterpret_cast<float*>(acc) + 2 * off, (float)v, 1.0f);
+    } else {
+      AT::op(acc + off, v);
+      if (CNT) atomicAdd(cnt + off, 1);
+    }
   };
 
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if (VEC) {
-    // 1-D, contiguous index (int64) and src, 16-byte aligned: 4 elements / thread
+    // 1-D, contiguous index (int64) and src, 16-byte aligned: quads of 4
+    // elements, grid-strided; the next quad is loaded while this one updates
     static_assert(!VEC || sizeof(I) == 8, "vector path expects int64 index");
     const int64_t nq = n / 4;
-    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nq; q += stride) {
-      const uint4 i01 = ld_global_stream_v4(index + q * 4);
-      const uint4 i23 = ld_global_stream_v4(index + q * 4 + 2);
+    struct Quad {
+      uint4 i01, i23;
       T sv[4];
-      if (sizeof(T) == 4) {
+    };
+    auto load_quad = [&](int64_t q, Quad& Q) {
+      if (q >= nq) return;
+      Q.i01 = ld_global_stream_v4(index + q * 4);
+      Q.i23 = ld_global_stream_v4(index + q * 4 + 2);
+      if constexpr (sizeof(T) == 4) {
         const uint4 s4 = ld_global_stream_v4(src + q * 4);
-        memcpy(sv, &s4, 16);
+        memcpy(Q.sv, &s4, 16);
       } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sv[e] = src[q * 4 + e];
+        for (int e = 0; e < 4; ++e) Q.sv[e] = src[q * 4 + e];
       }
+    };
+    auto do_quad = [&](const Quad& Q) {
       int64_t iv[4];
-      iv[0] = (int64_t)(((uint64_t)i01.y << 32) | i01.x);
-      iv[1] = (int64_t)(((uint64_t)i01.w << 32) | i01.z);
-      iv[2] = (int64_t)(((uint64_t)i23.y << 32) | i23.x);
-      iv[3] = (int64_t)(((uint64_t)i23.w << 32) | i23.z);
+      iv[0] = (int64_t)(((uint64_t)Q.i01.y << 32) | Q.i01.x);
+      iv[1] = (int64_t)(((uint64_t)Q.i01.w << 32) | Q.i01.z);
+      iv[2] = (int64_t)(((uint64_t)Q.i23.y << 32) | Q.i23.x);
+      iv[3] = (int64_t)(((uint64_t)Q.i23.w << 32) | Q.i23.z);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         if (iv[e] < 0 || iv[e] >= g.out_dim) { ++bad; continue; }
-        update(iv[e] * g.ostr[0], AT::from(sv[e]));
+        update(iv[e] * g.ostr[0], AT::from(Q.sv[e]));
       }
+    };
+    Quad qa, qb;
+    int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    load_quad(q, qa);
+    for (; q < nq; q += 2 * stride) {
+      load_quad(q + stride, qb);
+      do_quad(qa);
+      if (q + stride >= nq) break;
+      load_quad(q + 2 * stride, qa);
+      do_quad(qb);
     }
     for (int64_t p = nq * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += stride) {
       const int64_t iv = (int64_t)index[p];
@@ -253,8 +289,12 @@ scatter_kernel(const T* __restrict__ src, const I* __restrict__ index,
     for (int j = threadIdx.x; j < kSlots; j += blockDim.x) {
       const uint32_t t = s_tag[j];
       if (t != kEmpty) {
-        AT::op(acc + t, s_val[j]);
-        if (CNT) atomicAdd(cnt + t, s_cnt[j]);
+        if constexpr (PAIR) {
+          red_pair(reinterpret_cast<float*>(acc) + 2 * (int64_t)t, (float)s_val[j], (float)s_cnt[j]);
+        } else {
+          AT::op(acc + t, s_val[j]);
+          if (CNT) atomicAdd(cnt + t, s_cnt[j]);
+        }
       }
     }
   }
@@ -279,7 +319,7 @@ __device__ __forceinline__ int64_t out_offset(const OutGeo& o, int64_t i) {
   return off;
 }
 
-template <typename T, int OP, bool KEYS>
+template <typename T, int OP, bool KEYS, bool PAIR>
 __global__ void scatter_init_kernel(const T* __restrict__ out, typename Acc<T, OP, KEYS>::A* acc,
                                     int32_t* cnt, OutGeo o, bool include_self) {
   using AT = Acc<T, OP, KEYS>;
@@ -287,15 +327,20 @@ __global__ void scatter_init_kernel(const T* __restrict__ out, typename Acc<T, O
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t off = out_offset(o, i);
     // the accumulator is indexed by the out offset (same strides as out)
-    acc[off] = include_self ? AT::from(out[off]) : AT::identity();
-    if (cnt) cnt[off] = 0;
+    if constexpr (PAIR) {
+      reinterpret_cast<float2*>(acc)[off] =
+          make_float2(include_self ? (float)AT::from(out[off]) : 0.f, 0.f);
+    } else {
+      acc[off] = include_self ? AT::from(out[off]) : AT::identity();
+      if (cnt) cnt[off] = 0;
+    }
   }
 }
 
 template <typename T> __device__ __forceinline__ T from_acc(float a) { return from_f<T>(a); }
 template <> __device__ __forceinline__ int32_t from_acc<int32_t>(float a) { return (int32_t)a; }
 
-template <typename T, int OP, bool KEYS>
+template <typename T, int OP, bool KEYS, bool PAIR>
 __global__ void scatter_finalize_kernel(T* __restrict__ out,
                                         const typename Acc<T, OP, KEYS>::A* __restrict__ acc,
                                         const int32_t* __restrict__ cnt, OutGeo o,
@@ -311,9 +356,17 @@ __global__ void scatter_finalize_kernel(T* __restrict__ out,
       out[off] = from_f<T>(funkey(k));
       continue;
     } else {
-    const int32_t c = cnt ? cnt[off] : 1;
+    A a;
+    int32_t c;
+    if constexpr (PAIR) {
+      const float2 pr = reinterpret_cast<const float2*>(acc)[off];
+      a = (A)pr.x;
+      c = (int32_t)pr.y;
+    } else {
+      c = cnt ? cnt[off] : 1;
+      a = acc_is_out ? (A)0 : acc[off];
+    }
     if (!include_self && c == 0) continue;  // never reached: keeps self
-    A a = acc_is_out ? (A)0 : acc[off];
     if (OP == kMean) {
       const int32_t den = include_self ? c + 1 : c;
       if constexpr (std::is_same<A, float>::value) {
@@ -343,8 +396,15 @@ struct Plan {
   bool keys;     // float amax/amin via uint32 keys in scratch
   bool scratch;  // accumulator in scratch (else directly in out)
   bool counts;   // int32 counts in scratch
+  bool pair;     // interleaved float (sum, count) pairs in scratch (set per call)
   size_t acc_bytes, cnt_bytes;
 };
+
+// Float sum without self and float mean may use (sum, count) pairs; the
+// workspace covers both that layout and separate float sums + int32 counts.
+inline bool pair_capable(int reduce, bool include_self, int dtype) {
+  return is_float(dtype) && (reduce == FO_MEAN || (reduce == FO_SUM && !include_self));
+}
 
 Plan make_plan(int reduce, bool include_self, int dtype, int64_t span) {
   Plan p{};
@@ -352,11 +412,16 @@ Plan make_plan(int reduce, bool include_self, int dtype, int64_t span) {
   const bool half = dtype == FO_F16 || dtype == FO_BF16;
   p.keys = f && (reduce == FO_AMAX || reduce == FO_AMIN);
   p.counts = (reduce == FO_MEAN) || (!include_self && !p.keys);
-  p.scratch = p.keys || !include_self || half;
+  p.scratch = p.keys || !include_self || half || pair_capable(reduce, include_self, dtype);
   size_t asz = p.keys ? 4 : (f ? 4 : dtype_size(dtype));
   p.acc_bytes = p.scratch ? round256((size_t)span * asz) : 0;
   p.cnt_bytes = p.counts ? round256((size_t)span * 4) : 0;
   return p;
+}
+
+// Per-call choice: pairs when every count fits a float exactly (<= 2^24 updates).
+inline void choose_pairs(Plan& p, int reduce, bool include_self, int dtype, int64_t n) {
+  p.pair = pair_capable(reduce, include_self, dtype) && n <= ((int64_t)1 << 24);
 }
 
 // number of elements an out-offset-indexed array must cover
@@ -375,14 +440,20 @@ int run(void* out, const void* src, const void* index, const Geo& g, const OutGe
   using AT = Acc<T, OP, KEYS>;
   using A = typename AT::A;
   A* acc = pl.scratch ? reinterpret_cast<A*>(ws) : reinterpret_cast<A*>(out);
-  int32_t* cnt = pl.counts ? reinterpret_cast<int32_t*>((char*)ws + pl.acc_bytes) : nullptr;
+  int32_t* cnt = (pl.counts && !pl.pair) ? reinterpret_cast<int32_t*>((char*)ws + pl.acc_bytes)
+                                         : nullptr;
+  constexpr bool kPairable = std::is_same<A, float>::value && !KEYS && (OP == kSum || OP == kMean);
   const int sms = num_sms();
   if (pl.scratch) {
     int64_t gi = (og.numel + 255) / 256;
     if (gi > sms * 8) gi = sms * 8;
     if (gi < 1) gi = 1;
-    scatter_init_kernel<T, OP, KEYS><<<(unsigned)gi, 256, 0, st>>>((const T*)out, acc, cnt, og,
-                                                                    include_self);
+    if (kPairable && pl.pair)
+      scatter_init_kernel<T, OP, KEYS, kPairable><<<(unsigned)gi, 256, 0, st>>>(
+          (const T*)out, acc, nullptr, og, include_self);
+    else
+      scatter_init_kernel<T, OP, KEYS, false><<<(unsigned)gi, 256, 0, st>>>((const T*)out, acc, cnt,
+                                                                           og, include_self);
     if (int rc = check_launch("scatter_init_kernel")) return rc;
   } else if (cnt) {
     cudaMemsetAsync(cnt, 0, pl.cnt_bytes, st);
@@ -396,12 +467,21 @@ int run(void* out, const void* src, const void* index, const Geo& g, const OutGe
     const bool vec = g.ndim == 1 && sizeof(I) == 8 && g.istr[0] == 1 && g.sstr[0] == 1 &&
                      aligned16(index) && aligned16(src);
 #define FO_LAUNCH(ND, V)                                                                       \
-  scatter_kernel<T, I, OP, KEYS, true, ND, V><<<(unsigned)grid, kThreads, 0, st>>>(            \
+  scatter_kernel<T, I, OP, KEYS, true, false, ND, V><<<(unsigned)grid, kThreads, 0, st>>>(     \
       (const T*)src, (const I*)index, acc, cnt, n, g, err, use_cache)
 #define FO_LAUNCH_NC(ND, V)                                                                    \
-  scatter_kernel<T, I, OP, KEYS, false, ND, V><<<(unsigned)grid, kThreads, 0, st>>>(           \
+  scatter_kernel<T, I, OP, KEYS, false, false, ND, V><<<(unsigned)grid, kThreads, 0, st>>>(    \
       (const T*)src, (const I*)index, acc, nullptr, n, g, err, use_cache)
-    if (cnt) {
+#define FO_LAUNCH_PAIR(ND, V)                                                                  \
+  scatter_kernel<T, I, OP, KEYS, false, kPairable, ND, V><<<(unsigned)grid, kThreads, 0, st>>>( \
+      (const T*)src, (const I*)index, acc, nullptr, n, g, err, use_cache)
+    if (kPairable && pl.pair) {
+      if (vec) FO_LAUNCH_PAIR(1, (sizeof(I) == 8));
+      else if (g.ndim == 1) FO_LAUNCH_PAIR(1, false);
+      else if (g.ndim == 2) FO_LAUNCH_PAIR(2, false);
+      else if (g.ndim == 3) FO_LAUNCH_PAIR(3, false);
+      else FO_LAUNCH_PAIR(4, false);
+    } else if (cnt) {
       if (vec) FO_LAUNCH(1, (sizeof(I) == 8));
       else if (g.ndim == 1) FO_LAUNCH(1, false);
       else if (g.ndim == 2) FO_LAUNCH(2, false);
@@ -416,14 +496,19 @@ int run(void* out, const void* src, const void* index, const Geo& g, const OutGe
     }
 #undef FO_LAUNCH
 #undef FO_LAUNCH_NC
+#undef FO_LAUNCH_PAIR
     if (int rc = check_launch("scatter_kernel")) return rc;
   }
   if (pl.scratch || OP == kMean) {
     int64_t gf = (og.numel + 255) / 256;
     if (gf > sms * 8) gf = sms * 8;
     if (gf < 1) gf = 1;
-    scatter_finalize_kernel<T, OP, KEYS><<<(unsigned)gf, 256, 0, st>>>(
-        (T*)out, acc, cnt, og, include_self, !pl.scratch);
+    if (kPairable && pl.pair)
+      scatter_finalize_kernel<T, OP, KEYS, kPairable><<<(unsigned)gf, 256, 0, st>>>(
+          (T*)out, acc, nullptr, og, include_self, false);
+    else
+      scatter_finalize_kernel<T, OP, KEYS, false><<<(unsigned)gf, 256, 0, st>>>(
+          (T*)out, acc, cnt, og, include_self, !pl.scratch);
     if (int rc = check_launch("scatter_finalize_kernel")) return rc;
   }
   return FO_OK;
@@ -517,7 +602,8 @@ extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, 
   if (og.numel == 0) return FO_OK;
   FO_CHECK_ARG(out && (n == 0 || (src && index)), "scatter_reduce: null pointer");
   const int64_t span = out_span(og.shape, og.str, ndim);
-  const Plan pl = make_plan(reduce, include_self != 0, dtype, span);
+  Plan pl = make_plan(reduce, include_self != 0, dtype, span);
+  choose_pairs(pl, reduce, include_self != 0, dtype, n);
   if ((int64_t)(pl.acc_bytes + pl.cnt_bytes) > 0 &&
       (!workspace || ws_bytes < (int64_t)(pl.acc_bytes + pl.cnt_bytes))) {
     set_error("scatter_reduce: workspace of %lld bytes required, got %lld",
