@@ -210,3 +210,41 @@ def test_empty_batch():
     t = torch.empty(0, dtype=torch.long, device=DEV)
     assert fused_cross_entropy(x, t, reduction="sum").item() == 0
     assert fused_cross_entropy(x, t, reduction="none").shape == (0,)
+
+
+@pytest.mark.parametrize("dtype,V", [(torch.bfloat16, 16384), (torch.bfloat16, 128256),
+                                     (torch.bfloat16, 262144), (torch.float16, 65536),
+                                     (torch.float32, 8192), (torch.float32, 131072)])
+@pytest.mark.parametrize("ls", [0.0, 0.1])
+def test_long_rows_fused_grad(dtype, V, ls):
+    """Rows long enough for the cluster kernel (the row split over 1-8 CTAs),
+    with ignored rows, label smoothing and a target in the last column."""
+    g = torch.Generator().manual_seed(V)
+    B = 12
+    logits = (torch.randn(B, V, generator=g) * 2).to(dtype)
+    target = torch.randint(0, V, (B,), generator=g)
+    target[3] = -100
+    target[7] = V - 1
+    target[8] = 0
+    for red in ("mean", "sum"):
+        loss, grad = _run(logits, target, reduction=red, label_smoothing=ls)
+        rl, rg = _ref(logits, target, reduction=red, label_smoothing=ls)
+        if dtype == torch.float32:
+            _close(loss, rl, dtype, "loss")
+        else:
+            torch.testing.assert_close(loss.float(), rl.float(), rtol=2e-2, atol=0)
+        _close(grad, rg, dtype, f"grad {red}")
+        assert torch.all(grad[3] == 0)
+
+
+def test_long_rows_strided_logits():
+    """Rows of a wider buffer (row stride > V) through the fused gradient."""
+    base = (torch.randn(6, 40000) * 2).bfloat16()
+    logits = base[:, :32768]
+    target = torch.randint(0, 32768, (6,))
+    x = logits.to(DEV).requires_grad_(True)
+    loss = fused_cross_entropy(x, target.to(DEV))
+    loss.backward()
+    rl, rg = _ref(logits.contiguous(), target)
+    torch.testing.assert_close(loss.detach().cpu().float(), rl.float(), rtol=2e-2, atol=0)
+    _close(x.grad.cpu(), rg, torch.bfloat16, "grad")
