@@ -118,9 +118,12 @@ def scatter_inputs():
 SCATTER_BYTES = (1 << 24) * 4 + (1 << 24) * 8 + (1 << 20) * 4 * 2
 
 
+CE_ROWS = 8192   # --ce-batch: a smaller batch of the same rows, for profiler captures
+
+
 def ce_inputs():
     g = _gen(0)
-    B, V = 8192, 128256
+    B, V = CE_ROWS, 128256
     logits = (2.0 * torch.randn(B, V, generator=g)).bfloat16()
     target = torch.randint(0, V, (B,), generator=g)
     target[torch.rand(B, generator=g) < 0.05] = -100
@@ -455,10 +458,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-per-op", action="store_true", help="headline only")
+    ap.add_argument("--ce-batch", type=int, default=8192,
+                    help="rows of the cross-entropy workload (default: the benchmark's 8192)")
     ap.add_argument("--only", default=None,
                     help="run one per-op workload (rms_norm_fp32, median_c, scatter, ce, "
                          "delta, ...) and print its entry; used for profiler captures")
     args = ap.parse_args()
+    global CE_ROWS
+    CE_ROWS = args.ce_batch
     if args.warmup < 3:
         args.warmup = 3
 

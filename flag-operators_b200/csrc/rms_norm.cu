@@ -49,16 +49,25 @@ rms_fwd_vec_kernel(const T* __restrict__ x, const W* __restrict__ w, T* __restri
     }
   };
 
-  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+  // The next row's loads are issued before this row's block reduction, so they
+  // are in flight while the CTA waits at the barrier and stores (rows of up to
+  // 4 vectors per thread; longer rows have no registers to spare for it).
+  auto load_row = [&](int64_t row, uint4 (&dst)[VPT]) {
     const T* xr = x + row * (int64_t)N;
-    T* yr = y + row * (int64_t)N;
-    uint4 raw[VPT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int v = threadIdx.x + i * blockDim.x;
-      if (v < nvec) raw[i] = ld_global_stream_v4(xr + (int64_t)v * E);
-      else raw[i] = make_uint4(0, 0, 0, 0);
+      if (v < nvec) dst[i] = ld_global_stream_v4(xr + (int64_t)v * E);
+      else dst[i] = make_uint4(0, 0, 0, 0);
     }
+  };
+  uint4 raw[VPT];
+  if (blockIdx.x < M) load_row(blockIdx.x, raw);
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    T* yr = y + row * (int64_t)N;
+    constexpr bool kPrefetch = VPT <= 4;
+    uint4 nxt[VPT];
+    if (kPrefetch && row + gridDim.x < M) load_row(row + gridDim.x, nxt);
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -81,6 +90,12 @@ rms_fwd_vec_kernel(const T* __restrict__ x, const W* __restrict__ w, T* __restri
         for (int e = 0; e < E; ++e) f[e] = (f[e] * inv) * weight(i, e, v);
         st_global_stream_v4(yr + (int64_t)v * E, pack16<T>(f));
       }
+    }
+    if (kPrefetch) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) raw[i] = nxt[i];
+    } else if (row + gridDim.x < M) {
+      load_row(row + gridDim.x, raw);
     }
   }
 }
