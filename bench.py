@@ -101,6 +101,13 @@ def rms_bytes(x):
     return 2 * M * N * e + N * e + M * 4
 
 
+def rms_bwd_bytes(x):
+    """read x, dy, inv_rms, weight; write dx, dw."""
+    M, N = x.shape
+    e = x.element_size()
+    return 3 * M * N * e + 2 * N * e + M * 4
+
+
 def scatter_inputs():
     g = _gen(0)
     n_self, n_src = 1 << 20, 1 << 24
@@ -295,7 +302,7 @@ def cpu_entry(fn, nbytes_or_units, unit, sample, kind="port", per="GB/s"):
 def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
     import oracle
     from operators.median import median
-    from operators.rms_norm import rms_norm_forward
+    from operators.rms_norm import rms_norm_backward, rms_norm_forward
     from operators.scatter_reduce import scatter_reduce
     from operators.fused_cross_entropy import fused_cross_entropy
     from operators.chunk_gated_delta_rule import chunk_gated_delta_rule
@@ -322,6 +329,27 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
         res[f"rms_norm_{cfg}"] = hbm_entry(f"rms_norm_{cfg}", rms_bytes(x), ms, K, 1, hbm, src,
                                            traffic, cpu)
         del xd, wd
+
+    # rms_norm backward (dx, dw) from inv_rms
+    for cfg in ("fp32", "bf16"):
+        if not want(f"rms_norm_bwd_{cfg}"):
+            continue
+        x, w = rms_inputs(cfg)
+        dy = torch.randn(x.shape, generator=_gen(1)).to(x.dtype)
+        xd, wd, dyd = x.to(dev), w.to(dev), dy.to(dev)
+        _, invd = rms_norm_forward(xd, (xd.shape[1],), wd, 1e-6)
+        ms = time_steps(lambda: rms_norm_backward(dyd, xd, invd, (xd.shape[1],), wd), K, W, flush,
+                        dist)
+        cpu = None
+        if do_cpu:
+            rows = 1024
+            cpu = cpu_entry(lambda: oracle.rms_norm_backward(dy[:rows], x[:rows], (x.shape[1],), w,
+                                                             1e-6),
+                            rms_bwd_bytes(x[:rows]), "GB/s",
+                            f"first {rows} of {x.shape[0]} rows (autograd through the CPU formula)")
+        res[f"rms_norm_bwd_{cfg}"] = hbm_entry(f"rms_norm_bwd_{cfg}", rms_bwd_bytes(x), ms, K, 2, hbm,
+                                               src, traffic, cpu)
+        del xd, wd, dyd, invd
 
     # median a, b, c (a is also the headline)
     for cfg in (("a", "b", "c") if only else ("b", "c")):

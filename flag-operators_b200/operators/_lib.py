@@ -37,6 +37,9 @@ _i64p = ctypes.POINTER(ctypes.c_int64)
 _SIGS = {
     "fo_rms_norm_fwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _f32,
                         _int, _int, _c_void_p],
+    "fo_rms_norm_bwd_workspace_bytes": [_i64, _i64, _i64p],
+    "fo_rms_norm_bwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64,
+                        _i64, _int, _int, _c_void_p, _i64, _c_void_p],
     "fo_median_dim": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _int, _c_void_p],
     "fo_median_all_workspace_bytes": [_i64, _i64p],
     "fo_median_all": [_c_void_p, _c_void_p, _i64, _int, _c_void_p, _i64, _c_void_p],

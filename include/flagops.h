@@ -80,6 +80,21 @@ FO_API int fo_rms_norm_fwd(const void* x, const void* weight, void* y, float* in
                     int64_t M, int64_t N, float eps, int x_dtype, int w_dtype,
                     void* stream);
 
+/*
+ * rms_norm backward from the forward's inv_rms (dy, x, dx: [M, N] x_dtype; weight, dw: [N]
+ * w_dtype; inv_rms: [M] fp32):
+ *   dx = inv * (dy * w) - x * inv^3 * sum_j(dy_j w_j x_j) / N,   dw = sum_m dy * x * inv
+ * Scratch: fo_rms_norm_bwd_workspace_bytes(M, N) bytes (dw partial sums).  The reference
+ * returns inv_rms "for backward" (operators/rms_norm.py:10,17,186-228; its API is the
+ * FlagGems one) and has no backward kernel of its own; this is the backward of its CPU
+ * formula (rms_norm.py:211-216).
+ */
+FO_API int fo_rms_norm_bwd_workspace_bytes(int64_t M, int64_t N, int64_t* bytes);
+FO_API int fo_rms_norm_bwd(const void* dy, const void* x, const void* weight,
+                           const float* inv_rms, void* dx, void* dw, int64_t M, int64_t N,
+                           int x_dtype, int w_dtype, void* workspace, int64_t ws_bytes,
+                           void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* median                                                                    */
 /* ------------------------------------------------------------------------ */

@@ -14,6 +14,7 @@ tests).  Parity is therefore pinned to the reference itself.
 """
 from .ops import (  # noqa: F401
     rms_norm_forward,
+    rms_norm_backward,
     median,
     median_dim_np,
     scatter_reduce_,

@@ -42,6 +42,24 @@ def rms_norm_forward(x, normalized_shape, weight, eps=1e-5):
     return y, inv_rms
 
 
+def rms_norm_backward(dy, x, normalized_shape, weight, eps=1e-5):
+    """(dx, dw) of the CPU forward of rms_norm.py:211-213 by autograd, in fp32.
+
+    The reference has no backward of its own; its forward returns inv_rms for a
+    backward (rms_norm.py:10-17), whose result is the gradient of this formula.
+    """
+    x = _cpu(x).float().clone().requires_grad_(True)
+    w = _cpu(weight).float().clone().requires_grad_(True)
+    if isinstance(normalized_shape, int):
+        normalized_shape = (normalized_shape,)
+    N = math.prod(normalized_shape)
+    xf = x.view(-1, N)
+    rms = torch.sqrt((xf * xf).mean(dim=-1, keepdim=True) + eps)
+    y = (xf / rms) * w.view(-1)
+    y.backward(_cpu(dy).float().view(-1, N))
+    return x.grad.detach(), w.grad.detach()
+
+
 # ---------------------------------------------------------------------------
 # median — operators/median.py:348-352 (CPU branch: torch.median)
 # ---------------------------------------------------------------------------

@@ -147,3 +147,21 @@ def test_delta_rule_oracle_final_state_chains():
                                        g[:, :, s:], initial_state=h1, output_final_state=True)
     assert torch.allclose(torch.cat([o1, o2], 2), o, atol=1e-5)
     assert torch.allclose(h2, h, atol=1e-5)
+
+
+def test_rms_norm_backward_oracle_matches_the_analytic_gradient():
+    """The oracle's backward (autograd through the reference's CPU formula)
+    against an independent float64 statement of the gradient."""
+    g = torch.Generator().manual_seed(7)
+    M, N, eps = 16, 96, 1e-5
+    x = torch.randn(M, N, generator=g) * 1.5
+    w = 1 + 0.3 * torch.randn(N, generator=g)
+    dy = torch.randn(M, N, generator=g)
+    dx, dw = oracle.rms_norm_backward(dy, x, (N,), w, eps)
+    xd, wd, dyd = (t.double().numpy() for t in (x, w, dy))
+    inv = 1.0 / np.sqrt((xd * xd).mean(axis=1, keepdims=True) + eps)
+    gg = dyd * wd
+    dx_ref = inv * gg - xd * inv ** 3 * (gg * xd).sum(axis=1, keepdims=True) / N
+    dw_ref = (dyd * xd * inv).sum(axis=0)
+    np.testing.assert_allclose(dx.numpy(), dx_ref, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(dw.numpy(), dw_ref, rtol=1e-5, atol=1e-5)

@@ -158,3 +158,82 @@ def test_empty_rows():
     x = torch.empty(0, 64, device=DEV)
     y, inv = rms_norm_forward(x, (64,), torch.ones(64, device=DEV))
     assert y.shape == (0, 64) and inv.shape == (0,)
+
+
+# ---------------------------------------------------------------------------
+# backward (dx, dw) from inv_rms
+# ---------------------------------------------------------------------------
+def _bwd_case(M, N, dtype, wdtype=None, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(M, N, generator=g) * 1.5).to(dtype)
+    w = (1 + 0.3 * torch.randn(N, generator=g)).to(wdtype or dtype)
+    dy = torch.randn(M, N, generator=g).to(dtype)
+    return x, w, dy
+
+
+def _check_bwd(x, w, dy, eps=1e-6):
+    from operators.rms_norm import rms_norm_backward
+    N = x.shape[-1]
+    xd, wd, dyd = x.to(DEV), w.to(DEV), dy.to(DEV)
+    _, inv = rms_norm_forward(xd, (N,), wd, eps)
+    dx, dw = rms_norm_backward(dyd, xd, inv, (N,), wd)
+    assert dx.dtype == x.dtype and dw.dtype == w.dtype
+    rdx, rdw = oracle.rms_norm_backward(dy, x, (N,), w, eps)
+    if x.dtype == torch.float32:
+        torch.testing.assert_close(dx.cpu(), rdx, rtol=1e-5, atol=1e-5)
+    else:
+        torch.testing.assert_close(dx.cpu().float(), rdx, rtol=2e-2, atol=2e-2)
+    # dw sums M terms: its fp32 error is bounded by 1e-5 of the sum of their
+    # magnitudes; a 16-bit dw adds one rounding (2^-8 relative for bf16)
+    inv_c = inv.cpu()[:, None]
+    scale = (dy.float() * x.float() * inv_c).abs().sum(0)
+    tol = 1e-5 * scale + 1e-5
+    if w.dtype != torch.float32:
+        tol = tol + 8e-3 * rdw.abs()
+    err = (dw.cpu().float() - rdw).abs()
+    assert bool((err <= tol).all()), float(err.max())
+
+
+@pytest.mark.parametrize("M,N", [(64, 1024), (33, 4096), (257, 2048), (16, 96), (8, 100),
+                                 (5, 3000), (4, 16384)])
+def test_backward_float32(M, N):
+    _check_bwd(*_bwd_case(M, N, torch.float32))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("N", [1024, 4096, 8192, 8200, 16384])
+def test_backward_half(dtype, N):
+    _check_bwd(*_bwd_case(48, N, dtype, seed=N))
+
+
+def test_backward_mixed_weight_dtype():
+    _check_bwd(*_bwd_case(40, 2048, torch.bfloat16, torch.float32))
+
+
+def test_backward_benchmark_shape_bf16():
+    """[16384, 8192] bf16, the forward benchmark's shape."""
+    _check_bwd(*_bwd_case(16384, 8192, torch.bfloat16, seed=3))
+
+
+def test_autograd_through_rms_norm():
+    x, w, dy = _bwd_case(32, 512, torch.float32, seed=5)
+    xd = x.to(DEV).requires_grad_(True)
+    wd = w.to(DEV).requires_grad_(True)
+    y = rms_norm(xd, (512,), wd, 1e-6)
+    y.backward(dy.to(DEV))
+    rdx, rdw = oracle.rms_norm_backward(dy, x, (512,), w, 1e-6)
+    torch.testing.assert_close(xd.grad.cpu(), rdx, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(wd.grad.cpu(), rdw, rtol=1e-4, atol=1e-4)
+    # only x requires grad
+    xd2 = x.to(DEV).requires_grad_(True)
+    rms_norm(xd2, 512, w.to(DEV), 1e-6).backward(dy.to(DEV))
+    torch.testing.assert_close(xd2.grad.cpu(), rdx, rtol=1e-5, atol=1e-5)
+
+
+def test_backward_empty_rows():
+    from operators.rms_norm import rms_norm_backward
+    x = torch.empty(0, 64, device=DEV)
+    w = torch.randn(64, device=DEV)
+    dx, dw = rms_norm_backward(torch.empty(0, 64, device=DEV), x,
+                               torch.empty(0, device=DEV), (64,), w)
+    assert dx.shape == (0, 64) and torch.all(dw == 0)
