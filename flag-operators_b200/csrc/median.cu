@@ -1000,6 +1000,16 @@ extern "C" int fo_median_dim(const void* x, void* values, int64_t* indices, int6
   return FO_EDTYPE;
 }
 
+extern "C" int fo_median_timeouts(unsigned int* count) {
+  clear_error();
+  FO_CHECK_ARG(count, "fo_median_timeouts: null pointer");
+  if (cudaMemcpyFromSymbol(count, g_median_timeouts, sizeof(unsigned int)) != cudaSuccess) {
+    set_error("fo_median_timeouts: cannot read the device counter");
+    return FO_ECUDA;
+  }
+  return FO_OK;
+}
+
 extern "C" int fo_median_all_workspace_bytes(int64_t n, int64_t* bytes) {
   clear_error();
   FO_CHECK_ARG(bytes && n >= 0, "fo_median_all_workspace_bytes: bad argument");

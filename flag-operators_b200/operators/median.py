@@ -96,6 +96,14 @@ def median(inp: torch.Tensor, dim=None, keepdim: bool = False):
     return _median_dim(inp, dim, keepdim)
 
 
+def timeouts() -> int:
+    """Hand-off waits of the producer/consumer kernel that ran out of polls since
+    load (0 in a healthy run)."""
+    c = _lib.ctypes.c_uint(0)
+    _lib.call("fo_median_timeouts", _lib.ctypes.byref(c))
+    return int(c.value)
+
+
 def register_with_flaggems():
     """Registers median with FlagGems when it is installed (median.py:363-372)."""
     try:

@@ -269,6 +269,12 @@ FO_API int fo_gdr_fwd_stepwise(const void* q, const void* k, const void* v,
  * outputs incomplete).  Synchronous read of a device counter. */
 FO_API int fo_gdr_timeouts(unsigned int* count);
 
+/* Number of hand-off waits of the producer/consumer median kernel (rows of
+ * 1024 < N <= 2048) that ran out of polls since the library was loaded (0 in a
+ * healthy run; a timed-out CTA stops and leaves its remaining rows unwritten).
+ * Synchronous read of a device counter.  No reference counterpart. */
+FO_API int fo_median_timeouts(unsigned int* count);
+
 /* Operand-layout self-test of the tensor-core path (no reference counterpart):
  * d[128, N] (fp32) = A[128, K] . B[N, K]^T on one CTA with tcgen05.mma, bf16 A/B.
  * a is [128][K] (a_mn = 0, K-major) or [K][128] (a_mn = 1); b is [N][K] (b_mn = 0)

@@ -169,3 +169,12 @@ def test_int32_full_rows(N):
     x[2] = 2**31 - 1
     x[3:10] = torch.randint(-3, 3, (7, N), generator=g).to(torch.int32)
     _exact(x)
+
+
+def test_no_handoff_timeouts():
+    """Collected after the median tests above: none of their producer/consumer
+    hand-offs ran out of polls."""
+    from operators.median import timeouts
+    median(torch.randn(300, 2048).to(DEV), dim=-1)
+    torch.cuda.synchronize()
+    assert timeouts() == 0
