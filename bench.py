@@ -366,6 +366,20 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
                                          traffic, cpu)
         del xd
 
+    # global median (dim=None) of the [8192, 2048] fp32 tensor: the grid-wide radix select
+    if want("median_global"):
+        x = median_inputs("a")
+        xd = x.to(dev)
+        ms = time_steps(lambda: median(xd), K, W, flush, dist)
+        cpu = None
+        if do_cpu:
+            xs = x[:1024]
+            cpu = cpu_entry(lambda: oracle.median(xs), xs.numel() * 4, "GB/s",
+                            "first 1024 of 8192 rows, flattened")
+        res["median_global"] = hbm_entry("median_global", x.numel() * 4 + 4, ms, K, 9, hbm, src,
+                                         traffic, cpu)
+        del xd
+
     # scatter_reduce
     if want("scatter"):
         self_, srcv, idx_u, idx_z, src_i = scatter_inputs()

@@ -910,6 +910,207 @@ median_cta_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __rest
 }
 
 // ---------------------------------------------------------------------------
+// global median of n >= 2^20 elements: the whole grid per radix pass
+// ---------------------------------------------------------------------------
+// Every CTA owns a contiguous chunk of x.  Per pass, each CTA histograms the
+// digit of its chunk's elements that match the prefix selected so far into
+// shared memory and adds its non-empty bins to a global histogram; one CTA
+// then picks the bin holding rank r and clears the histogram.  After the last
+// pass the key is known; each CTA counts its elements with that key, and one
+// CTA walks the chunk holding the r-th such element in index order (the stable
+// rule).  The first NaN (lowest index) decides a row holding any NaN.
+constexpr int kGmThreads = 512;
+constexpr int kGmBins = 2048;
+constexpr int kGmMaxCtas = 1024;
+constexpr int64_t kGmMinN = (int64_t)1 << 20;
+
+struct GmState {
+  unsigned long long prefix, mask, r, first_nan;
+};
+
+__global__ void gm_init_kernel(GmState* s, uint32_t* hist, int64_t k) {
+  if (threadIdx.x == 0) {
+    s->prefix = 0;
+    s->mask = 0;
+    s->r = (unsigned long long)k;
+    s->first_nan = ~0ull;
+  }
+  for (int j = threadIdx.x; j < kGmBins; j += blockDim.x) hist[j] = 0;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGmThreads)
+gm_hist_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
+               uint32_t* __restrict__ hist, int p) {
+  using Tr = KeyTraits<T>;
+  using K = typename Tr::K;
+  using D = Digits<K>;
+  __shared__ uint32_t h[kGmBins];
+  if (p > 0 && *(volatile unsigned long long*)&s->first_nan != ~0ull) return;  // NaN decided
+  const K prefix = (K)s->prefix, mask = (K)s->mask;
+  const int sh = D::shift(p);
+  const uint32_t nb = 1u << D::width(p), dmask = nb - 1u;
+  for (uint32_t j = threadIdx.x; j < nb; j += kGmThreads) h[j] = 0;
+  __syncthreads();
+  const int64_t j0 = (int64_t)blockIdx.x * chunk;
+  const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
+  unsigned long long my_nan = ~0ull;
+  for (int64_t j = j0 + threadIdx.x; j < j1; j += kGmThreads) {
+    const T v = x[j];
+    if (p == 0 && Tr::isnan_(v) && (unsigned long long)j < my_nan) my_nan = (unsigned long long)j;
+    const K kk = Tr::key(v);
+    if ((kk & mask) == prefix) atomicAdd(h + ((uint32_t)(kk >> sh) & dmask), 1u);
+  }
+  if (p == 0 && my_nan != ~0ull) atomicMin(&s->first_nan, my_nan);
+  __syncthreads();
+  for (uint32_t j = threadIdx.x; j < nb; j += kGmThreads)
+    if (h[j]) atomicAdd(hist + j, h[j]);
+}
+
+// One CTA of 1024 threads (2 bins each): the bin holding rank r.
+template <typename T>
+__global__ void __launch_bounds__(1024) gm_find_kernel(GmState* s, uint32_t* hist, int p) {
+  using K = typename KeyTraits<T>::K;
+  using D = Digits<K>;
+  __shared__ uint32_t wsum[32];
+  __shared__ uint32_t s_bin, s_below;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const uint32_t c0 = hist[2 * tid], c1 = hist[2 * tid + 1];
+  __syncthreads();
+  hist[2 * tid] = 0;
+  hist[2 * tid + 1] = 0;
+  if (s->first_nan != ~0ull) return;
+  const uint32_t tot = c0 + c1;
+  uint32_t inc = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) wsum[wid] = inc;
+  __syncthreads();
+  uint32_t off = 0;
+  for (int q = 0; q < wid; ++q) off += wsum[q];
+  const uint64_t exc = (uint64_t)off + inc - tot;
+  const uint64_t r = s->r;
+  if (exc <= r && r < exc + tot) {
+    if (r < exc + c0) {
+      s_bin = 2 * tid;
+      s_below = (uint32_t)exc;
+    } else {
+      s_bin = 2 * tid + 1;
+      s_below = (uint32_t)(exc + c0);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const int sh = D::shift(p);
+    const uint32_t dmask = (1u << D::width(p)) - 1u;
+    s->r = r - s_below;
+    s->prefix |= (unsigned long long)((K)s_bin << sh);
+    s->mask |= (unsigned long long)((K)dmask << sh);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGmThreads)
+gm_count_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, const GmState* s,
+                uint32_t* __restrict__ cnt) {
+  using Tr = KeyTraits<T>;
+  using K = typename Tr::K;
+  __shared__ uint32_t red[kGmThreads / 32];
+  if (s->first_nan != ~0ull) return;
+  const K key = (K)s->prefix;
+  const int64_t j0 = (int64_t)blockIdx.x * chunk;
+  const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
+  uint32_t c = 0;
+  for (int64_t j = j0 + threadIdx.x; j < j1; j += kGmThreads) c += (Tr::key(x[j]) == key) ? 1u : 0u;
+  c = __reduce_add_sync(0xffffffffu, c);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int q = 0; q < kGmThreads / 32; ++q) t += red[q];
+    cnt[blockIdx.x] = t;
+  }
+}
+
+// One CTA: the chunk holding the r-th element with the selected key, then the
+// element itself in index order.
+template <typename T>
+__global__ void __launch_bounds__(kGmThreads)
+gm_pick_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, const GmState* s,
+               const uint32_t* __restrict__ cnt, int G, T* __restrict__ value) {
+  using Tr = KeyTraits<T>;
+  using K = typename Tr::K;
+  __shared__ uint32_t wsum[kGmThreads / 32];
+  __shared__ int s_cta;
+  __shared__ unsigned long long s_r;
+  __shared__ long long s_found;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (s->first_nan != ~0ull) {
+    if (tid == 0) *value = x[s->first_nan];
+    return;
+  }
+  if (tid == 0) {
+    unsigned long long r = s->r;
+    int c = 0;
+    while (c < G - 1 && r >= cnt[c]) {
+      r -= cnt[c];
+      ++c;
+    }
+    s_cta = c;
+    s_r = r;
+    s_found = -1;
+  }
+  __syncthreads();
+  const K key = (K)s->prefix;
+  const int64_t j0 = (int64_t)s_cta * chunk;
+  const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
+  unsigned long long r = s_r;
+  for (int64_t base = j0; base < j1; base += kGmThreads) {
+    const int64_t j = base + tid;
+    const bool m = j < j1 && Tr::key(x[j]) == key;
+    const uint32_t bal = __ballot_sync(0xffffffffu, m);
+    if (lane == 0) wsum[wid] = __popc(bal);
+    __syncthreads();
+    uint32_t off = 0, tot = 0;
+    for (int q = 0; q < kGmThreads / 32; ++q) {
+      const uint32_t c = wsum[q];
+      if (q < wid) off += c;
+      tot += c;
+    }
+    const uint32_t rank = off + __popc(bal & ((1u << lane) - 1u));
+    if (m && (unsigned long long)rank == r) s_found = j;
+    __syncthreads();
+    if (s_found >= 0 || r < tot) break;
+    r -= tot;
+  }
+  if (tid == 0) *value = s_found >= 0 ? x[s_found] : x[j0];
+}
+
+template <typename T>
+int launch_grid_median(const void* xv, void* value, int64_t n, void* ws, cudaStream_t st) {
+  using K = typename KeyTraits<T>::K;
+  const T* x = (const T*)xv;
+  GmState* s = reinterpret_cast<GmState*>(ws);
+  uint32_t* hist = reinterpret_cast<uint32_t*>((char*)ws + 256);
+  uint32_t* cnt = hist + kGmBins;
+  int64_t G = (int64_t)num_sms() * 2;
+  if (G > kGmMaxCtas) G = kGmMaxCtas;
+  const int64_t chunk = (n + G - 1) / G;
+  G = (n + chunk - 1) / chunk;
+  gm_init_kernel<<<1, 256, 0, st>>>(s, hist, (n - 1) / 2);
+  for (int p = 0; p < Digits<K>::kPasses; ++p) {
+    gm_hist_kernel<T><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p);
+    gm_find_kernel<T><<<1, 1024, 0, st>>>(s, hist, p);
+  }
+  gm_count_kernel<T><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, cnt);
+  gm_pick_kernel<T><<<1, kGmThreads, 0, st>>>(x, n, chunk, s, cnt, (int)G, (T*)value);
+  return check_launch("global median");
+}
+
+// ---------------------------------------------------------------------------
 // dispatch
 // ---------------------------------------------------------------------------
 template <typename T, int RG, int VW, bool FULL>
@@ -1013,7 +1214,9 @@ extern "C" int fo_median_timeouts(unsigned int* count) {
 extern "C" int fo_median_all_workspace_bytes(int64_t n, int64_t* bytes) {
   clear_error();
   FO_CHECK_ARG(bytes && n >= 0, "fo_median_all_workspace_bytes: bad argument");
-  *bytes = 8;  // the index of the selected element
+  // small n: the index of the selected element (one CTA); large n: the grid
+  // path's state, histogram and per-CTA counts
+  *bytes = n >= kGmMinN ? (int64_t)(256 + 4 * (kGmBins + kGmMaxCtas)) : 8;
   return FO_OK;
 }
 
@@ -1027,6 +1230,21 @@ extern "C" int fo_median_all(const void* x, void* value, int64_t n, int dtype, v
     return FO_EWORKSPACE;
   }
   cudaStream_t st = as_stream(stream);
+  if (n >= kGmMinN && n < ((int64_t)1 << 32)) {
+    int64_t need = 0;
+    fo_median_all_workspace_bytes(n, &need);
+    if (ws_bytes < need) {
+      set_error("median: workspace of %lld bytes required", (long long)need);
+      return FO_EWORKSPACE;
+    }
+    switch (dtype) {
+      case FO_F32: return launch_grid_median<float>(x, value, n, workspace, st);
+      case FO_F16: return launch_grid_median<__half>(x, value, n, workspace, st);
+      case FO_BF16: return launch_grid_median<__nv_bfloat16>(x, value, n, workspace, st);
+      case FO_I32: return launch_grid_median<int32_t>(x, value, n, workspace, st);
+      case FO_I64: return launch_grid_median<int64_t>(x, value, n, workspace, st);
+    }
+  }
   int64_t* idx = reinterpret_cast<int64_t*>(workspace);
   switch (dtype) {
     case FO_F32: return launch_cta<float>(x, value, idx, 1, n, st);

@@ -81,9 +81,11 @@ def _median_global(inp: torch.Tensor) -> torch.Tensor:
     orig_dtype = inp.dtype
     x = _prep(inp).reshape(-1).contiguous()
     out = torch.empty((), dtype=x.dtype, device=x.device)
-    ws = torch.empty(1, dtype=torch.int64, device=x.device)
+    nbytes = _lib.ctypes.c_int64(0)
+    _lib.call("fo_median_all_workspace_bytes", x.numel(), _lib.ctypes.byref(nbytes))
+    ws = torch.empty((nbytes.value + 7) // 8, dtype=torch.int64, device=x.device)
     _lib.call("fo_median_all", _lib.ptr(x), _lib.ptr(out), x.numel(), _lib.dtype_code(x.dtype),
-              _lib.ptr(ws), 8, _lib.stream_of(x))
+              _lib.ptr(ws), nbytes.value, _lib.stream_of(x))
     return out.to(orig_dtype)
 
 

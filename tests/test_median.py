@@ -178,3 +178,43 @@ def test_no_handoff_timeouts():
     median(torch.randn(300, 2048).to(DEV), dim=-1)
     torch.cuda.synchronize()
     assert timeouts() == 0
+
+
+@pytest.mark.parametrize("case", ["randn", "ties", "const", "nan", "zeros", "int32", "int64",
+                                  "bf16", "fp16", "odd"])
+def test_global_median_grid_path(case):
+    """n >= 2^20 elements: the grid-wide radix select (a CTA per chunk per pass)."""
+    g = torch.Generator().manual_seed(11)
+    n = 1 << 21
+    if case == "randn":
+        x = torch.randn(8192, 2048, generator=g)
+    elif case == "ties":
+        x = torch.randint(-5, 5, (n,), generator=g).float()
+    elif case == "const":
+        x = torch.full((n,), 2.5)
+    elif case == "nan":
+        x = torch.randn(n, generator=g)
+        x[n - 7] = float("nan")
+        x[123457] = float("nan")
+    elif case == "zeros":
+        x = torch.where(torch.rand(n, generator=g) < 0.5, torch.tensor(-0.0), torch.tensor(0.0))
+        x[:1000] = 1.0
+        x[-1000:] = -1.0
+    elif case == "int32":
+        x = torch.randint(-2**31, 2**31 - 1, (n,), generator=g, dtype=torch.int64).to(torch.int32)
+    elif case == "int64":
+        x = torch.randint(-2**62, 2**62, (n,), generator=g, dtype=torch.int64)
+    elif case == "bf16":
+        x = torch.randn(n, generator=g).bfloat16()
+    elif case == "fp16":
+        x = torch.randn(n, generator=g).half()
+    else:
+        x = torch.randn((1 << 20) + 13, generator=g)
+    got = median(x.to(DEV)).cpu()
+    ref = oracle.median(x)
+    if case == "nan":
+        assert torch.isnan(got).item()
+    else:
+        assert torch.equal(got, ref), (got, ref)
+    from operators.median import timeouts
+    assert timeouts() == 0
