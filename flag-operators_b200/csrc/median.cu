@@ -89,6 +89,10 @@ template <> struct KeyTraits<int64_t> {
   using K = uint64_t;
   static __device__ __forceinline__ K key(int64_t x) { return (uint64_t)x ^ 0x8000000000000000ull; }
   static __device__ __forceinline__ bool isnan_(int64_t) { return false; }
+  static __device__ __forceinline__ bool is_zero_key(uint64_t) { return false; }
+  static __device__ __forceinline__ int64_t from_key(uint64_t k) {
+    return (int64_t)(k ^ 0x8000000000000000ull);
+  }
 };
 
 template <typename K> struct Digits {
@@ -916,17 +920,64 @@ median_cta_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __rest
 // digit of its chunk's elements that match the prefix selected so far into
 // shared memory and adds its non-empty bins to a global histogram; one CTA
 // then picks the bin holding rank r and clears the histogram.  After the last
-// pass the key is known; each CTA counts its elements with that key, and one
-// CTA walks the chunk holding the r-th such element in index order (the stable
-// rule).  The first NaN (lowest index) decides a row holding any NaN.
+// pass the key is known and gives the value, except for the key that +0.0 and
+// -0.0 share: then each CTA counts its zeros and one CTA walks the chunk holding
+// the r-th zero in index order and returns it, sign included.  The first NaN
+// (lowest index) decides an input holding any NaN.
 constexpr int kGmThreads = 512;
 constexpr int kGmBins = 2048;
 constexpr int kGmMaxCtas = 1024;
+static_assert(kGmMaxCtas <= 2 * kGmThreads, "gm_pick_kernel scans two counts per thread");
 constexpr int64_t kGmMinN = (int64_t)1 << 20;
 
 struct GmState {
   unsigned long long prefix, mask, r, first_nan;
 };
+
+// Calls f(j, x[j]) for every j in [j0, j1) of the calling CTA.  When x + j0 is
+// 16-byte aligned: 16-byte loads in batches of 4 per thread, software-pipelined
+// (the next batch is in flight while the current one is processed); element
+// loads for the ragged end, and for the whole range otherwise.
+template <typename T, typename F>
+__device__ __forceinline__ void gm_for_chunk(const T* __restrict__ x, int64_t j0, int64_t j1, F&& f) {
+  constexpr int E = 16 / (int)sizeof(T);
+  constexpr int U = 4;
+  constexpr int64_t kStep = (int64_t)U * kGmThreads;
+  int64_t js = j0;
+  if ((reinterpret_cast<uintptr_t>(x + j0) & 15) == 0) {
+    const int64_t nv = (j1 - j0) / E;
+    const uint4* __restrict__ xv = reinterpret_cast<const uint4*>(x + j0);
+    auto load = [&](uint4* r, int64_t v) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (v + u * kGmThreads < nv) r[u] = __ldg(xv + v + u * kGmThreads);
+    };
+    auto proc = [&](const uint4* r, int64_t v) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (v + u * kGmThreads < nv) {
+          T e[E];
+          memcpy(e, &r[u], 16);
+#pragma unroll
+          for (int i = 0; i < E; ++i) f(j0 + (v + u * kGmThreads) * E + i, e[i]);
+        }
+    };
+    uint4 ra[U], rb[U];
+    int64_t v = threadIdx.x;
+    if (v < nv) load(ra, v);
+    while (v < nv) {
+      if (v + kStep < nv) load(rb, v + kStep);
+      proc(ra, v);
+      v += kStep;
+      if (v >= nv) break;
+      if (v + kStep < nv) load(ra, v + kStep);
+      proc(rb, v);
+      v += kStep;
+    }
+    js = j0 + nv * E;
+  }
+  for (int64_t j = js + threadIdx.x; j < j1; j += kGmThreads) f(j, x[j]);
+}
 
 __global__ void gm_init_kernel(GmState* s, uint32_t* hist, int64_t k) {
   if (threadIdx.x == 0) {
@@ -938,7 +989,8 @@ __global__ void gm_init_kernel(GmState* s, uint32_t* hist, int64_t k) {
   for (int j = threadIdx.x; j < kGmBins; j += blockDim.x) hist[j] = 0;
 }
 
-template <typename T>
+// P0: the first pass (every element counts; NaNs are looked for)
+template <typename T, bool P0>
 __global__ void __launch_bounds__(kGmThreads)
 gm_hist_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
                uint32_t* __restrict__ hist, int p) {
@@ -946,7 +998,7 @@ gm_hist_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
   using K = typename Tr::K;
   using D = Digits<K>;
   __shared__ uint32_t h[kGmBins];
-  if (p > 0 && *(volatile unsigned long long*)&s->first_nan != ~0ull) return;  // NaN decided
+  if (!P0 && *(volatile unsigned long long*)&s->first_nan != ~0ull) return;  // NaN decided
   const K prefix = (K)s->prefix, mask = (K)s->mask;
   const int sh = D::shift(p);
   const uint32_t nb = 1u << D::width(p), dmask = nb - 1u;
@@ -955,13 +1007,16 @@ gm_hist_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
   const int64_t j0 = (int64_t)blockIdx.x * chunk;
   const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
   unsigned long long my_nan = ~0ull;
-  for (int64_t j = j0 + threadIdx.x; j < j1; j += kGmThreads) {
-    const T v = x[j];
-    if (p == 0 && Tr::isnan_(v) && (unsigned long long)j < my_nan) my_nan = (unsigned long long)j;
-    const K kk = Tr::key(v);
-    if ((kk & mask) == prefix) atomicAdd(h + ((uint32_t)(kk >> sh) & dmask), 1u);
-  }
-  if (p == 0 && my_nan != ~0ull) atomicMin(&s->first_nan, my_nan);
+  gm_for_chunk<T>(x, j0, j1, [&](int64_t j, T v) {
+    if (P0) {
+      if (Tr::isnan_(v) && (unsigned long long)j < my_nan) my_nan = (unsigned long long)j;
+      atomicAdd(h + ((uint32_t)(Tr::key(v) >> sh) & dmask), 1u);
+    } else {
+      const K kk = Tr::key(v);
+      if ((kk & mask) == prefix) atomicAdd(h + ((uint32_t)(kk >> sh) & dmask), 1u);
+    }
+  });
+  if (P0 && my_nan != ~0ull) atomicMin(&s->first_nan, my_nan);
   __syncthreads();
   for (uint32_t j = threadIdx.x; j < nb; j += kGmThreads)
     if (h[j]) atomicAdd(hist + j, h[j]);
@@ -1021,10 +1076,11 @@ gm_count_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, const GmState
   __shared__ uint32_t red[kGmThreads / 32];
   if (s->first_nan != ~0ull) return;
   const K key = (K)s->prefix;
+  if (!Tr::is_zero_key(key)) return;  // the key alone gives the value
   const int64_t j0 = (int64_t)blockIdx.x * chunk;
   const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
   uint32_t c = 0;
-  for (int64_t j = j0 + threadIdx.x; j < j1; j += kGmThreads) c += (Tr::key(x[j]) == key) ? 1u : 0u;
+  gm_for_chunk<T>(x, j0, j1, [&](int64_t, T v) { c += (Tr::key(v) == key) ? 1u : 0u; });
   c = __reduce_add_sync(0xffffffffu, c);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = c;
   __syncthreads();
@@ -1052,19 +1108,41 @@ gm_pick_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, const GmState*
     if (tid == 0) *value = x[s->first_nan];
     return;
   }
+  const K key = (K)s->prefix;
+  if (!Tr::is_zero_key(key)) {
+    if (tid == 0) *value = Tr::from_key(key);
+    return;
+  }
+  // +0.0 and -0.0 share the key: the chunk holding the r-th zero, from a
+  // block-wide inclusive scan of the per-CTA counts (two per thread).
+  __shared__ unsigned long long wtot[kGmThreads / 32];
+  const unsigned long long r0 = s->r;
+  const uint32_t a0 = (2 * tid < G) ? cnt[2 * tid] : 0u;
+  const uint32_t a1 = (2 * tid + 1 < G) ? cnt[2 * tid + 1] : 0u;
+  unsigned long long inc = (unsigned long long)a0 + a1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) wtot[wid] = inc;
   if (tid == 0) {
-    unsigned long long r = s->r;
-    int c = 0;
-    while (c < G - 1 && r >= cnt[c]) {
-      r -= cnt[c];
-      ++c;
-    }
-    s_cta = c;
-    s_r = r;
+    s_cta = G - 1;
+    s_r = 0;
     s_found = -1;
   }
   __syncthreads();
-  const K key = (K)s->prefix;
+  unsigned long long before = 0;
+  for (int q = 0; q < wid; ++q) before += wtot[q];
+  const unsigned long long ex = before + inc - a0 - a1;  // zeros in the chunks before 2*tid
+  if (r0 >= ex && r0 < ex + a0) {
+    s_cta = 2 * tid;
+    s_r = r0 - ex;
+  } else if (r0 >= ex + a0 && r0 < ex + a0 + a1) {
+    s_cta = 2 * tid + 1;
+    s_r = r0 - ex - a0;
+  }
+  __syncthreads();
   const int64_t j0 = (int64_t)s_cta * chunk;
   const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
   unsigned long long r = s_r;
@@ -1098,11 +1176,15 @@ int launch_grid_median(const void* xv, void* value, int64_t n, void* ws, cudaStr
   uint32_t* cnt = hist + kGmBins;
   int64_t G = (int64_t)num_sms() * 2;
   if (G > kGmMaxCtas) G = kGmMaxCtas;
-  const int64_t chunk = (n + G - 1) / G;
+  // chunks of a multiple of 2048 elements keep every chunk start 16-byte aligned
+  const int64_t chunk = ((n + G - 1) / G + 2047) / 2048 * 2048;
   G = (n + chunk - 1) / chunk;
   gm_init_kernel<<<1, 256, 0, st>>>(s, hist, (n - 1) / 2);
   for (int p = 0; p < Digits<K>::kPasses; ++p) {
-    gm_hist_kernel<T><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p);
+    if (p == 0)
+      gm_hist_kernel<T, true><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p);
+    else
+      gm_hist_kernel<T, false><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p);
     gm_find_kernel<T><<<1, 1024, 0, st>>>(s, hist, p);
   }
   gm_count_kernel<T><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, cnt);

@@ -181,7 +181,7 @@ def test_no_handoff_timeouts():
 
 
 @pytest.mark.parametrize("case", ["randn", "ties", "const", "nan", "zeros", "int32", "int64",
-                                  "bf16", "fp16", "odd"])
+                                  "bf16", "fp16", "odd", "offset", "zeros_bf16"])
 def test_global_median_grid_path(case):
     """n >= 2^20 elements: the grid-wide radix select (a CTA per chunk per pass)."""
     g = torch.Generator().manual_seed(11)
@@ -208,13 +208,27 @@ def test_global_median_grid_path(case):
         x = torch.randn(n, generator=g).bfloat16()
     elif case == "fp16":
         x = torch.randn(n, generator=g).half()
+    elif case == "zeros_bf16":
+        x = torch.where(torch.rand(n, generator=g) < 0.3, torch.tensor(-0.0), torch.tensor(0.0))
+        x[:5000] = -2.0
+        x = x.bfloat16()
+    elif case == "offset":
+        x = torch.randn(n + 3, generator=g)
     else:
         x = torch.randn((1 << 20) + 13, generator=g)
-    got = median(x.to(DEV)).cpu()
-    ref = oracle.median(x)
+    if case == "offset":
+        # a view starting 12 bytes into its storage: element loads instead of 16-byte loads
+        got = median(x.to(DEV)[3:]).cpu()
+        ref = oracle.median(x[3:])
+    else:
+        got = median(x.to(DEV)).cpu()
+        ref = oracle.median(x)
     if case == "nan":
         assert torch.isnan(got).item()
     else:
+        # torch's global median is the element std::nth_element leaves at rank k;
+        # between +0.0 and -0.0 that choice is unspecified, so a zero median is
+        # compared by value (the kernel returns an input zero, with its sign)
         assert torch.equal(got, ref), (got, ref)
     from operators.median import timeouts
     assert timeouts() == 0
