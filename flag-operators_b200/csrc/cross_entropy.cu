@@ -30,6 +30,36 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// packed fp32x2 arithmetic: one instruction for two lanes (sm_100a)
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&r);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
+// Sum of E (even, >= 4) floats as a tree of packed additions.
+template <int E>
+__device__ __forceinline__ float sum_vec(const float* e) {
+  float2 p[E / 2];
+#pragma unroll
+  for (int i = 0; i < E / 2; ++i) p[i] = make_float2(e[2 * i], e[2 * i + 1]);
+#pragma unroll
+  for (int w = 1; w < E / 2; w <<= 1)
+#pragma unroll
+    for (int i = 0; i + w < E / 2; i += 2 * w) p[i] = add2(p[i], p[i + w]);
+  return p[0].x + p[0].y;
+}
+
 struct MS {
   float m;  // running max
   float s;  // sum of exp(x - m)
@@ -51,21 +81,20 @@ __device__ __forceinline__ void ms_add_vec(MS& st, float& rsum, const float* f, 
     st.m = lm;
   }
   if (st.m != -INFINITY) {
-    // tree sum of the vector, then one add into the running sum (short dependency chain)
-    const float mb = st.m * kLog2e;
+    // arguments two at a time, tree sum of the vector, then one add into the
+    // running sum (short dependency chain)
+    const float mb = -st.m * kLog2e;
+    const float2 l2 = make_float2(kLog2e, kLog2e), b2 = make_float2(mb, mb);
     float e[E];
 #pragma unroll
-    for (int i = 0; i < E; ++i) e[i] = fast_exp2(fmaf(f[i], kLog2e, -mb));
-#pragma unroll
-    for (int w = 1; w < E; w <<= 1)
-#pragma unroll
-      for (int i = 0; i + w < E; i += 2 * w) e[i] += e[i + w];
-    st.s += e[0];
+    for (int i = 0; i < E; i += 2) {
+      const float2 a = fma2(make_float2(f[i], f[i + 1]), l2, b2);
+      e[i] = fast_exp2(a.x);
+      e[i + 1] = fast_exp2(a.y);
+    }
+    st.s += sum_vec<E>(e);
   }
-  if (ls) {
-#pragma unroll
-    for (int i = 0; i < E; ++i) rsum += f[i];
-  }
+  if (ls) rsum += sum_vec<E>(f);
 }
 
 __device__ __forceinline__ void ms_add_scalar(MS& st, float& rsum, float f, bool ls) {
@@ -140,6 +169,22 @@ __device__ __forceinline__ void row_stats(const T* __restrict__ p, int64_t n, bo
     ms_add_scalar(st, rsum, to_f<T>(p[j]), ls);
 }
 
+// f[i] <- scale * exp2(f[i] * log2 e - lb) - se, two lanes per instruction;
+// the same roundings as the scalar form (fused multiply-adds, ex2.approx).
+template <int E>
+__device__ __forceinline__ void grad_vec(float* f, float lb, float scale, float se) {
+  const float2 l2 = make_float2(kLog2e, kLog2e), b2 = make_float2(-lb, -lb);
+  const float2 s2 = make_float2(scale, scale), c2 = make_float2(-se, -se);
+#pragma unroll
+  for (int i = 0; i < E; i += 2) {
+    const float2 a = fma2(make_float2(f[i], f[i + 1]), l2, b2);
+    const float2 ex = make_float2(fast_exp2(a.x), fast_exp2(a.y));
+    const float2 g = fma2(s2, ex, c2);
+    f[i] = g.x;
+    f[i + 1] = g.y;
+  }
+}
+
 // Writes g[j] = scale * (exp(x[j] - lse) - eps_v - (1-e)[j + col0 == t]) for j < n.
 // scale == 0 (ignored row) writes zeros without reading x.
 template <typename T>
@@ -174,10 +219,13 @@ __device__ __forceinline__ void row_grad(const T* __restrict__ p, T* __restrict_
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       float f[E];
-      if (scale != 0.f) unpack16<T>(r[u], f);
-      const int64_t j0 = head + (v + u * blockDim.x) * E;
+      if (scale != 0.f) {
+        unpack16<T>(r[u], f);
+        grad_vec<E>(f, lb, scale, se);
+      } else {
 #pragma unroll
-      for (int i = 0; i < E; ++i) f[i] = one(j0 + i, scale != 0.f ? f[i] : 0.f);
+        for (int i = 0; i < E; ++i) f[i] = 0.f;
+      }
       st_global_stream_v4(gv + (v + u * blockDim.x) * E, pack16<T>(f));
     }
   }
