@@ -75,6 +75,7 @@ template <typename T, int OP> struct Acc<T, OP, true> {
     if (OP == kAmax) atomicMax(p, v);
     else atomicMin(p, v);
   }
+  static __device__ __forceinline__ A comb(A a, A b) { return OP == kAmax ? max(a, b) : min(a, b); }
 };
 
 template <typename A> __device__ __forceinline__ void atomic_add_a(A* p, A v);
@@ -146,7 +147,36 @@ template <typename T, int OP> struct Acc<T, OP, false> {
       else atomic_min_a((int64_t*)p, (int64_t)v);
     }
   }
+  // the same reduction of two values (warp aggregation before an atomic)
+  static __device__ __forceinline__ A comb(A a, A b) {
+    if (OP == kSum || OP == kMean) return a + b;
+    if (OP == kProd) return a * b;
+    if (OP == kAmax) return a > b ? a : b;
+    return a < b ? a : b;
+  }
 };
+
+// One compare-and-swap step of a product update: returns the cell's old value
+// and sets ok when it equalled `assumed` (bitwise), i.e. the product was stored.
+__device__ __forceinline__ float cas_mul(float* p, float assumed, float v, bool& ok) {
+  const unsigned int a = __float_as_uint(assumed);
+  const unsigned int o =
+      atomicCAS(reinterpret_cast<unsigned int*>(p), a, __float_as_uint(assumed * v));
+  ok = (o == a);
+  return __uint_as_float(o);
+}
+__device__ __forceinline__ int32_t cas_mul(int32_t* p, int32_t assumed, int32_t v, bool& ok) {
+  const int o = atomicCAS(p, assumed, (int)((uint32_t)assumed * (uint32_t)v));
+  ok = (o == assumed);
+  return o;
+}
+__device__ __forceinline__ int64_t cas_mul(int64_t* p, int64_t assumed, int64_t v, bool& ok) {
+  const unsigned long long a = (unsigned long long)assumed;
+  const unsigned long long o = atomicCAS(reinterpret_cast<unsigned long long*>(p), a,
+                                         (unsigned long long)((uint64_t)assumed * (uint64_t)v));
+  ok = (o == a);
+  return (int64_t)o;
+}
 template <typename T, int OP>
 __device__ __forceinline__ typename Acc<T, OP, false>::A Acc<T, OP, false>::from(T v) {
   if constexpr (std::is_same<A, float>::value) return tof<T>(v);
@@ -189,27 +219,31 @@ scatter_kernel(const T* __restrict__ src, const I* __restrict__ index,
   }
   int32_t bad = 0;
 
-  auto update = [&](int64_t off, A v) {
-    if (use_cache) {
-      const uint32_t o32 = (uint32_t)off;
-      const uint32_t slot = (o32 * 2654435761u) >> (32 - Slots<A>::kLog);
-      uint32_t t = s_tag[slot];
-      if (t == kEmpty) {
-        const uint32_t prev = atomicCAS(&s_tag[slot], kEmpty, o32);
-        t = (prev == kEmpty) ? o32 : prev;
-      }
-      if (t == o32) {
-        AT::op(&s_val[slot], v);
-        if (kCnt) atomicAdd(&s_cnt[slot], 1);
-        return;
-      }
+  // c: how many updates v stands for (warp-aggregated updates carry c > 1)
+  auto cache_update = [&](int64_t off, A v, int c) -> bool {
+    const uint32_t o32 = (uint32_t)off;
+    const uint32_t slot = (o32 * 2654435761u) >> (32 - Slots<A>::kLog);
+    uint32_t t = s_tag[slot];
+    if (t == kEmpty) {
+      const uint32_t prev = atomicCAS(&s_tag[slot], kEmpty, o32);
+      t = (prev == kEmpty) ? o32 : prev;
     }
+    if (t != o32) return false;
+    AT::op(&s_val[slot], v);
+    if (kCnt) atomicAdd(&s_cnt[slot], c);
+    return true;
+  };
+  auto global_update = [&](int64_t off, A v, int c) {
     if constexpr (PAIR) {
-      red_pair(reinterpret_cast<float*>(acc) + 2 * off, (float)v, 1.0f);
+      red_pair(reinterpret_cast<float*>(acc) + 2 * off, (float)v, (float)c);
     } else {
       AT::op(acc + off, v);
-      if (CNT) atomicAdd(cnt + off, 1);
+      if (CNT) atomicAdd(cnt + off, c);
     }
+  };
+  auto update = [&](int64_t off, A v) {
+    if (use_cache && cache_update(off, v, 1)) return;
+    global_update(off, v, 1);
   };
 
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -234,27 +268,97 @@ scatter_kernel(const T* __restrict__ src, const I* __restrict__ index,
         for (int e = 0; e < 4; ++e) Q.sv[e] = src[q * 4 + e];
       }
     };
-    auto do_quad = [&](const Quad& Q) {
+    // Every lane of a warp runs the same iterations (lanes past the end pass
+    // valid = false), so the warp can aggregate: lanes whose updates hit one
+    // cell are found with match.any; the lowest of them combines the others'
+    // values and issues one update carrying their count.  With skewed indices
+    // this turns several same-address atomics into one.  A warp keeps
+    // aggregating only if its first quad held at least 4 such duplicates
+    // (match.any costs more than it saves on spread-out indices).  Products
+    // that reach global memory are issued as a batch of independent
+    // compare-and-swaps.
+    const int lane = threadIdx.x & 31;
+    bool agg = use_cache, probing = use_cache;
+    auto do_quad = [&](const Quad& Q, bool valid) {
       int64_t iv[4];
       iv[0] = (int64_t)(((uint64_t)Q.i01.y << 32) | Q.i01.x);
       iv[1] = (int64_t)(((uint64_t)Q.i01.w << 32) | Q.i01.z);
       iv[2] = (int64_t)(((uint64_t)Q.i23.y << 32) | Q.i23.x);
       iv[3] = (int64_t)(((uint64_t)Q.i23.w << 32) | Q.i23.z);
+      int64_t off[4];
+      A val[4];
+      bool go[4];
+      int dups = 0;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        if (iv[e] < 0 || iv[e] >= g.out_dim) { ++bad; continue; }
-        update(iv[e] * g.ostr[0], AT::from(Q.sv[e]));
+        bool act = valid;
+        if (act && (iv[e] < 0 || iv[e] >= g.out_dim)) {
+          ++bad;
+          act = false;
+        }
+        off[e] = iv[e] * g.ostr[0];
+        A v = valid ? AT::from(Q.sv[e]) : AT::identity();
+        int c = 1;
+        if (agg) {  // warp-uniform; offsets fit 32 bits and never equal the sentinel
+          const uint32_t peers =
+              __match_any_sync(0xffffffffu, act ? (uint32_t)off[e] : 0xffffffffu);
+          const int lead = __ffs(peers) - 1;
+          const bool follower = act && lane != lead;
+          uint32_t fol = __ballot_sync(0xffffffffu, follower);
+          dups += __popc(fol);
+          while (fol) {  // warp-uniform: one shuffle per follower lane
+            const int src = __ffs(fol) - 1;
+            fol &= fol - 1;
+            const A ov = __shfl_sync(0xffffffffu, v, src);
+            if (act && lane == lead && ((peers >> src) & 1u)) v = AT::comb(v, ov);
+          }
+          if (follower) act = false;
+          c = __popc(peers);
+        }
+        val[e] = v;
+        go[e] = act && !(use_cache && cache_update(off[e], v, c));
+        if constexpr (OP != kProd || PAIR) {
+          if (go[e]) global_update(off[e], v, c);
+        } else if constexpr (CNT) {
+          if (go[e]) atomicAdd(cnt + off[e], c);  // the product itself is batched below
+        }
+      }
+      if (probing) {
+        agg = dups >= 4;
+        probing = false;
+      }
+      if constexpr (OP == kProd && !PAIR) {
+        __syncwarp();  // issue the batch from a converged warp
+        A old[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (go[e]) old[e] = *reinterpret_cast<volatile A*>(acc + off[e]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (go[e]) {
+            bool ok;
+            old[e] = cas_mul(acc + off[e], old[e], val[e], ok);
+            go[e] = !ok;
+          }
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          while (go[e]) {
+            bool ok;
+            old[e] = cas_mul(acc + off[e], old[e], val[e], ok);
+            go[e] = !ok;
+          }
       }
     };
     Quad qa, qb;
     int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t q0 = q - lane;  // the warp's first quad: loop bounds are warp-uniform
     load_quad(q, qa);
-    for (; q < nq; q += 2 * stride) {
+    for (int64_t w = q0; w < nq; w += 2 * stride, q += 2 * stride) {
       load_quad(q + stride, qb);
-      do_quad(qa);
-      if (q + stride >= nq) break;
+      do_quad(qa, q < nq);
+      if (w + stride >= nq) break;
       load_quad(q + 2 * stride, qa);
-      do_quad(qb);
+      do_quad(qb, q + stride < nq);
     }
     for (int64_t p = nq * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += stride) {
       const int64_t iv = (int64_t)index[p];
