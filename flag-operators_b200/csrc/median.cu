@@ -932,7 +932,28 @@ constexpr int64_t kGmMinN = (int64_t)1 << 20;
 
 struct GmState {
   unsigned long long prefix, mask, r, first_nan;
+  unsigned long long bin_cnt;  // elements in the bin selected by the last pass
+  unsigned int ovf;            // 1: the candidates of pass 1 were not (all) kept
 };
+
+// Geometry of the grid path: G CTAs with chunks of a multiple of 2048 elements
+// (every chunk start 16-byte aligned) and, per CTA, a region of R candidate
+// keys: pass 1 keeps the keys of the bin selected by pass 0 there, and later
+// passes read those instead of x when every CTA's candidates fit.
+struct GmGeo {
+  int64_t G, chunk, R;
+};
+inline GmGeo gm_geo(int64_t n) {
+  int64_t G = (int64_t)num_sms() * 2;
+  if (G > kGmMaxCtas) G = kGmMaxCtas;
+  const int64_t chunk = ((n + G - 1) / G + 2047) / 2048 * 2048;
+  G = (n + chunk - 1) / chunk;
+  const int64_t R = chunk < 8192 ? chunk : 8192;
+  return {G, chunk, R};
+}
+// workspace: state (256 B) | histogram | per-CTA counts | per-CTA candidate
+// counts | candidate regions (8 bytes per key, whatever the key width)
+constexpr int64_t kGmCandOff = 256 + 4 * (kGmBins + 2 * kGmMaxCtas);
 
 // Calls f(j, x[j]) for every j in [j0, j1) of the calling CTA.  When x + j0 is
 // 16-byte aligned: 16-byte loads in batches of 4 per thread, software-pipelined
@@ -985,38 +1006,79 @@ __global__ void gm_init_kernel(GmState* s, uint32_t* hist, int64_t k) {
     s->mask = 0;
     s->r = (unsigned long long)k;
     s->first_nan = ~0ull;
+    s->bin_cnt = 0;
+    s->ovf = 0;
   }
   for (int j = threadIdx.x; j < kGmBins; j += blockDim.x) hist[j] = 0;
 }
 
-// P0: the first pass (every element counts; NaNs are looked for)
-template <typename T, bool P0>
+// MODE 0: the first pass (every element counts; NaNs are looked for).
+// MODE 1: the second pass over x; also keeps the keys of the bin selected by
+//   pass 0 in this CTA's candidate region (when that bin fits all regions).
+// MODE 2: later passes; over this CTA's candidates when every CTA kept all of
+//   its own, else over x.
+template <typename T, int MODE>
 __global__ void __launch_bounds__(kGmThreads)
 gm_hist_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
-               uint32_t* __restrict__ hist, int p) {
+               uint32_t* __restrict__ hist, int p, typename KeyTraits<T>::K* __restrict__ cand,
+               uint32_t* __restrict__ ncand, int64_t R, int64_t G) {
   using Tr = KeyTraits<T>;
   using K = typename Tr::K;
   using D = Digits<K>;
   __shared__ uint32_t h[kGmBins];
-  if (!P0 && *(volatile unsigned long long*)&s->first_nan != ~0ull) return;  // NaN decided
+  __shared__ uint32_t s_nc;
+  if (MODE > 0 && *(volatile unsigned long long*)&s->first_nan != ~0ull) return;  // NaN decided
   const K prefix = (K)s->prefix, mask = (K)s->mask;
   const int sh = D::shift(p);
   const uint32_t nb = 1u << D::width(p), dmask = nb - 1u;
   for (uint32_t j = threadIdx.x; j < nb; j += kGmThreads) h[j] = 0;
+  if (threadIdx.x == 0) s_nc = 0;
   __syncthreads();
   const int64_t j0 = (int64_t)blockIdx.x * chunk;
   const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
+  const int lane = threadIdx.x & 31;
+  K* mine = cand + blockIdx.x * R;
   unsigned long long my_nan = ~0ull;
-  gm_for_chunk<T>(x, j0, j1, [&](int64_t j, T v) {
-    if (P0) {
+  if (MODE == 0) {
+    gm_for_chunk<T>(x, j0, j1, [&](int64_t j, T v) {
       if (Tr::isnan_(v) && (unsigned long long)j < my_nan) my_nan = (unsigned long long)j;
       atomicAdd(h + ((uint32_t)(Tr::key(v) >> sh) & dmask), 1u);
-    } else {
+    });
+    if (my_nan != ~0ull) atomicMin(&s->first_nan, my_nan);
+  } else if (MODE == 1) {
+    const bool keep = s->bin_cnt <= (unsigned long long)(G * R);
+    gm_for_chunk<T>(x, j0, j1, [&](int64_t, T v) {
       const K kk = Tr::key(v);
+      if ((kk & mask) == prefix) {
+        atomicAdd(h + ((uint32_t)(kk >> sh) & dmask), 1u);
+        if (keep) {  // append to this CTA's region, one shared atomic per group of lanes
+          const unsigned am = __activemask();
+          const int lead = __ffs(am) - 1;
+          uint32_t base = 0;
+          if (lane == lead) base = atomicAdd(&s_nc, (uint32_t)__popc(am));
+          base = __shfl_sync(am, base, lead);
+          const uint32_t q = base + (uint32_t)__popc(am & ((1u << lane) - 1u));
+          if (q < (uint32_t)R) mine[q] = kk;
+        }
+      }
+    });
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      ncand[blockIdx.x] = s_nc;
+      if (!keep || s_nc > (uint32_t)R) s->ovf = 1u;
+    }
+  } else if (!*(volatile unsigned int*)&s->ovf) {
+    const uint32_t m = ncand[blockIdx.x];
+    for (uint32_t q = threadIdx.x; q < m; q += kGmThreads) {
+      const K kk = mine[q];
       if ((kk & mask) == prefix) atomicAdd(h + ((uint32_t)(kk >> sh) & dmask), 1u);
     }
-  });
-  if (P0 && my_nan != ~0ull) atomicMin(&s->first_nan, my_nan);
+  } else {
+    gm_for_chunk<T>(x, j0, j1, [&](int64_t, T v) {
+      const K kk = Tr::key(v);
+      if ((kk & mask) == prefix) atomicAdd(h + ((uint32_t)(kk >> sh) & dmask), 1u);
+    });
+  }
   __syncthreads();
   for (uint32_t j = threadIdx.x; j < nb; j += kGmThreads)
     if (h[j]) atomicAdd(hist + j, h[j]);
@@ -1028,7 +1090,7 @@ __global__ void __launch_bounds__(1024) gm_find_kernel(GmState* s, uint32_t* his
   using K = typename KeyTraits<T>::K;
   using D = Digits<K>;
   __shared__ uint32_t wsum[32];
-  __shared__ uint32_t s_bin, s_below;
+  __shared__ uint32_t s_bin, s_below, s_cnt;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const uint32_t c0 = hist[2 * tid], c1 = hist[2 * tid + 1];
   __syncthreads();
@@ -1052,9 +1114,11 @@ __global__ void __launch_bounds__(1024) gm_find_kernel(GmState* s, uint32_t* his
     if (r < exc + c0) {
       s_bin = 2 * tid;
       s_below = (uint32_t)exc;
+      s_cnt = c0;
     } else {
       s_bin = 2 * tid + 1;
       s_below = (uint32_t)(exc + c0);
+      s_cnt = c1;
     }
   }
   __syncthreads();
@@ -1062,6 +1126,7 @@ __global__ void __launch_bounds__(1024) gm_find_kernel(GmState* s, uint32_t* his
     const int sh = D::shift(p);
     const uint32_t dmask = (1u << D::width(p)) - 1u;
     s->r = r - s_below;
+    s->bin_cnt = s_cnt;
     s->prefix |= (unsigned long long)((K)s_bin << sh);
     s->mask |= (unsigned long long)((K)dmask << sh);
   }
@@ -1174,17 +1239,21 @@ int launch_grid_median(const void* xv, void* value, int64_t n, void* ws, cudaStr
   GmState* s = reinterpret_cast<GmState*>(ws);
   uint32_t* hist = reinterpret_cast<uint32_t*>((char*)ws + 256);
   uint32_t* cnt = hist + kGmBins;
-  int64_t G = (int64_t)num_sms() * 2;
-  if (G > kGmMaxCtas) G = kGmMaxCtas;
-  // chunks of a multiple of 2048 elements keep every chunk start 16-byte aligned
-  const int64_t chunk = ((n + G - 1) / G + 2047) / 2048 * 2048;
-  G = (n + chunk - 1) / chunk;
+  uint32_t* ncand = cnt + kGmMaxCtas;
+  K* cand = reinterpret_cast<K*>((char*)ws + kGmCandOff);
+  const GmGeo geo = gm_geo(n);
+  const int64_t G = geo.G, chunk = geo.chunk, R = geo.R;
   gm_init_kernel<<<1, 256, 0, st>>>(s, hist, (n - 1) / 2);
   for (int p = 0; p < Digits<K>::kPasses; ++p) {
     if (p == 0)
-      gm_hist_kernel<T, true><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p);
+      gm_hist_kernel<T, 0><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p, cand,
+                                                               ncand, R, G);
+    else if (p == 1)
+      gm_hist_kernel<T, 1><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p, cand,
+                                                               ncand, R, G);
     else
-      gm_hist_kernel<T, false><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p);
+      gm_hist_kernel<T, 2><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p, cand,
+                                                               ncand, R, G);
     gm_find_kernel<T><<<1, 1024, 0, st>>>(s, hist, p);
   }
   gm_count_kernel<T><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, cnt);
@@ -1297,8 +1366,13 @@ extern "C" int fo_median_all_workspace_bytes(int64_t n, int64_t* bytes) {
   clear_error();
   FO_CHECK_ARG(bytes && n >= 0, "fo_median_all_workspace_bytes: bad argument");
   // small n: the index of the selected element (one CTA); large n: the grid
-  // path's state, histogram and per-CTA counts
-  *bytes = n >= kGmMinN ? (int64_t)(256 + 4 * (kGmBins + kGmMaxCtas)) : 8;
+  // path's state, histogram, per-CTA counts and candidate regions
+  if (n >= kGmMinN) {
+    const GmGeo geo = gm_geo(n);
+    *bytes = kGmCandOff + geo.G * geo.R * 8;
+  } else {
+    *bytes = 8;
+  }
   return FO_OK;
 }
 

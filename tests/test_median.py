@@ -181,7 +181,8 @@ def test_no_handoff_timeouts():
 
 
 @pytest.mark.parametrize("case", ["randn", "ties", "const", "nan", "zeros", "int32", "int64",
-                                  "bf16", "fp16", "odd", "offset", "zeros_bf16"])
+                                  "bf16", "fp16", "odd", "offset", "zeros_bf16", "const_4m",
+                                  "block_4m", "int64_4m"])
 def test_global_median_grid_path(case):
     """n >= 2^20 elements: the grid-wide radix select (a CTA per chunk per pass)."""
     g = torch.Generator().manual_seed(11)
@@ -214,6 +215,21 @@ def test_global_median_grid_path(case):
         x = x.bfloat16()
     elif case == "offset":
         x = torch.randn(n + 3, generator=g)
+    elif case == "const_4m":
+        # the median's bin holds every element: too many candidates to keep
+        x = torch.full((1 << 22,), -1.5)
+    elif case == "block_4m":
+        # the median's bin (values in [1, 1.25)) holds 20000 elements lying in one
+        # or two chunks of sorted data: they fit the candidate regions as a whole
+        # but overflow the CTAs that own them, so later passes read x again
+        m = 1 << 22
+        blk = 1.0 + 0.2 * torch.rand(20000, generator=g)
+        lo = m // 2 - 10000
+        x = torch.cat([torch.full((lo,), -2.0), blk.sort().values,
+                       torch.full((m - lo - 20000,), 3.0)])
+    elif case == "int64_4m":
+        # six passes: later ones read the kept candidates
+        x = torch.randint(-2**40, 2**40, (1 << 22,), generator=g, dtype=torch.int64)
     else:
         x = torch.randn((1 << 20) + 13, generator=g)
     if case == "offset":
