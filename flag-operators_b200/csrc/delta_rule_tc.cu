@@ -392,10 +392,9 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
             const bool on = (s <= tr) && (zr <= s);
             pv[j] = on ? -sg * sSB[s] * ex2(lt - sLc[s]) * __uint_as_float(r[j]) : 0.f;
           }
+          // stored transposed: sA[s][t] holds -A[t][s], so column s is contiguous
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4)
-            *reinterpret_cast<float4*>(sA + t * kAStride + 32 * hf + 4 * j4) =
-                make_float4(pv[4 * j4], pv[4 * j4 + 1], pv[4 * j4 + 2], pv[4 * j4 + 3]);
+          for (int j = 0; j < 32; ++j) sA[(32 * hf + j) * kAStride + t] = pv[j];
         }
       }
       // gQ, Kt and T overwrite chain inputs of chunk c - 1: wait for its last MMAs
@@ -404,53 +403,76 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       } else {
         gsync();
       }
-      if (p < 64) {
-        // ---- T = (I + A)^-1, one column per thread.  sA holds -A (zero on and
-        // above the diagonal), so T[i][j] = [i == j] + sum_{m<i} sA[i][m] T[m][j];
-        // the column is held as float2 pairs updated with packed fp32x2 FMAs.
-        const int j = p;
-        float2 col[kC / 2];
+      {
+        // ---- T = (I + A)^-1, two threads per column, right-looking: with
+        // N = -A (sA holds N transposed, zero on and above the diagonal), column
+        // j of T solves t_i = [i == j] + sum_{m<i} N[i][m] t_m.  Once t_i is
+        // final its contribution goes to every later row at once, so row i + 1 is
+        // final one FMA (and one shuffle) after row i.  Thread h of the pair
+        // holds the rows 8q + 4h + {0..3}; rows at or above i get N = 0 added.
+        const int j = p >> 1, h = p & 1;
+        float2 col[16];  // col[2q] = rows 8q+4h, +1; col[2q+1] = rows 8q+4h+2, +3
 #pragma unroll
-        for (int i = 0; i < kC / 2; ++i) col[i] = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int i = 0; i < kC; ++i) {
-          float2 acc0 = make_float2((i == j) ? 1.f : 0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-#pragma unroll
-          for (int m = 0; m < i; m += 4) {
-            const float4 a4 = *reinterpret_cast<const float4*>(sA + i * kAStride + m);
-            acc0 = fma2(make_float2(a4.x, a4.y), col[m / 2], acc0);
-            acc1 = fma2(make_float2(a4.z, a4.w), col[m / 2 + 1], acc1);
-          }
-          const float vv = (acc0.x + acc0.y) + (acc1.x + acc1.y);
-          if (i & 1) col[i / 2].y = vv;
-          else col[i / 2].x = vv;
+        for (int q = 0; q < 8; ++q) {
+          const int r0 = 8 * q + 4 * h;
+          col[2 * q] = make_float2(r0 == j ? 1.f : 0.f, r0 + 1 == j ? 1.f : 0.f);
+          col[2 * q + 1] = make_float2(r0 + 2 == j ? 1.f : 0.f, r0 + 3 == j ? 1.f : 0.f);
         }
-        // T -> fp16 tile [t][s] in the first half of the W^T buffer
 #pragma unroll
-        for (int i = 0; i < kC; ++i)
-          *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(i, j)) =
-              __float2half_rn((i & 1) ? col[i / 2].y : col[i / 2].x);
-      } else {
-        // ---- scaled copies: gQ -> GQ, Kt -> KT, gK in place
+        for (int i = 0; i < kC - 1; ++i) {
+          const int hi = (i >> 2) & 1, qi = i >> 3, ki = i & 3;
+          const float2 cv = col[2 * qi + (ki >> 1)];
+          const float mine = (ki & 1) ? cv.y : cv.x;  // row i, meaningful in thread hi
+          const float ti = __shfl_sync(0xffffffffu, mine, (lane & ~1) | hi);
+          const float2 t2 = make_float2(ti, ti);
+          const float* nc = sA + i * kAStride + 4 * h;  // N[8q + 4h + .][i]
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (8 * q + 7 <= i) continue;
+            const float4 a4 = *reinterpret_cast<const float4*>(nc + 8 * q);
+            col[2 * q] = fma2(make_float2(a4.x, a4.y), t2, col[2 * q]);
+            col[2 * q + 1] = fma2(make_float2(a4.z, a4.w), t2, col[2 * q + 1]);
+          }
+        }
+        // T -> fp16 tile [t][s] in the first half of the W^T buffer (own rows)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int r0 = 8 * q + 4 * h;
+          const float tv[4] = {col[2 * q].x, col[2 * q].y, col[2 * q + 1].x, col[2 * q + 1].y};
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(r0 + kk, j)) =
+                __float2half_rn(tv[kk]);
+        }
+      }
+      {
+        // ---- scaled copies: gQ -> GQ, Kt -> KT, gK in place; 8 loads in flight
         const float* sGam = reinterpret_cast<const float*>(G0 + G_GAM);
         const float* sGamP = reinterpret_cast<const float*>(G0 + G_GAMP);
         const float* sKts = reinterpret_cast<const float*>(G0 + G_KTS);
-#pragma unroll 2
-        for (int idx = p - 64; idx < 2048; idx += 64) {
-          const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
-          const int half = ch >> 3, cc = ch & 7;
-          if (m == 0) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(sm + OFF_QK + half * 16384 +
-                                                              tc::sw128_chunk(t, cc));
-            *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
-                scale8h(raw, __float2half2_rn(sGam[t]));
-          } else {
-            uint4* pp = reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 +
-                                                 tc::sw128_chunk(64 + t, cc));
-            const uint4 raw = *pp;
-            *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
-                scale8h(raw, __float2half2_rn(sKts[t]));
-            *pp = scale8h(raw, __float2half2_rn(sGamP[t]));
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {  // m = 0: Q rows (0-63), m = 1: K rows (64-127)
+          uint4 raw[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int rem = p + 128 * u, t = rem >> 4, ch = rem & 15;
+            raw[u] = *reinterpret_cast<const uint4*>(sm + OFF_QK + (ch >> 3) * 16384 +
+                                                     tc::sw128_chunk(64 * m + t, ch & 7));
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int rem = p + 128 * u, t = rem >> 4, ch = rem & 15;
+            const int half = ch >> 3, cc = ch & 7;
+            if (m == 0) {
+              *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
+                  scale8h(raw[u], __float2half2_rn(sGam[t]));
+            } else {
+              *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
+                  scale8h(raw[u], __float2half2_rn(sKts[t]));
+              *reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 +
+                                        tc::sw128_chunk(64 + t, cc)) =
+                  scale8h(raw[u], __float2half2_rn(sGamP[t]));
+            }
           }
         }
       }
