@@ -403,78 +403,133 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       } else {
         gsync();
       }
-      {
-        // ---- T = (I + A)^-1, two threads per column, right-looking: with
-        // N = -A (sA holds N transposed, zero on and above the diagonal), column
-        // j of T solves t_i = [i == j] + sum_{m<i} N[i][m] t_m.  Once t_i is
-        // final its contribution goes to every later row at once, so row i + 1 is
-        // final one FMA (and one shuffle) after row i.  Thread h of the pair
-        // holds the rows 8q + 4h + {0..3}; rows at or above i get N = 0 added.
-        const int j = p >> 1, h = p & 1;
-        float2 col[16];  // col[2q] = rows 8q+4h, +1; col[2q+1] = rows 8q+4h+2, +3
+      // ---- T = (I + A)^-1 by 32x32 blocks.  With N = -A (sA holds N
+      // transposed: sA[c][r] = N[r][c], zero on and above the diagonal),
+      // T = (I - N)^-1 has diagonal blocks T_II = (I - N_II)^-1 and
+      // T10 = T11 N10 T00.  The diagonal blocks are solved column by column
+      // (right-looking: once t_i is final its contribution goes to every later
+      // row, a 31-FMA dependency chain) by 64 threads while the other 64 make
+      // the scaled copies; then all 128 form P = N10 T00 and T10 = T11 P.
+      // Scratch: fp32 T00 | T11 in the P tile (free until the chain's next (f)),
+      // P in the unused upper triangle of sA.
+      float* Tsc = reinterpret_cast<float*>(sm + OFF_P);  // [2][32][32]
+      if (p < 64) {
+        const int I = p >> 5, cc = p & 31;
+        const float* nb = sA + (32 * I) * kAStride + 32 * I;  // nb[i][a] = N[32I+a][32I+i]
+        float2 col[16];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int r0 = 8 * q + 4 * h;
-          col[2 * q] = make_float2(r0 == j ? 1.f : 0.f, r0 + 1 == j ? 1.f : 0.f);
-          col[2 * q + 1] = make_float2(r0 + 2 == j ? 1.f : 0.f, r0 + 3 == j ? 1.f : 0.f);
-        }
+        for (int r = 0; r < 16; ++r)
+          col[r] = make_float2((2 * r == cc) ? 1.f : 0.f, (2 * r + 1 == cc) ? 1.f : 0.f);
 #pragma unroll
-        for (int i = 0; i < kC - 1; ++i) {
-          const int hi = (i >> 2) & 1, qi = i >> 3, ki = i & 3;
-          const float2 cv = col[2 * qi + (ki >> 1)];
-          const float mine = (ki & 1) ? cv.y : cv.x;  // row i, meaningful in thread hi
-          const float ti = __shfl_sync(0xffffffffu, mine, (lane & ~1) | hi);
+        for (int i = 0; i < 31; ++i) {
+          const float ti = (i & 1) ? col[i / 2].y : col[i / 2].x;
           const float2 t2 = make_float2(ti, ti);
-          const float* nc = sA + i * kAStride + 4 * h;  // N[8q + 4h + .][i]
+          const float* nc = nb + i * kAStride;
+          int r = i + 1;
+          if (r & 1) {  // row i + 1 shares its pair with the final row i
+            col[r / 2].y = fmaf(nc[r], ti, col[r / 2].y);
+            ++r;
+          }
+          if ((r & 3) && r < 32) {  // one pair up to a 4-row boundary
+            const float2 a2 = *reinterpret_cast<const float2*>(nc + r);
+            col[r / 2] = fma2(a2, t2, col[r / 2]);
+            r += 2;
+          }
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            if (8 * q + 7 <= i) continue;
-            const float4 a4 = *reinterpret_cast<const float4*>(nc + 8 * q);
-            col[2 * q] = fma2(make_float2(a4.x, a4.y), t2, col[2 * q]);
-            col[2 * q + 1] = fma2(make_float2(a4.z, a4.w), t2, col[2 * q + 1]);
+          for (; r < 32; r += 4) {
+            const float4 a4 = *reinterpret_cast<const float4*>(nc + r);
+            col[r / 2] = fma2(make_float2(a4.x, a4.y), t2, col[r / 2]);
+            col[r / 2 + 1] = fma2(make_float2(a4.z, a4.w), t2, col[r / 2 + 1]);
           }
         }
-        // T -> fp16 tile [t][s] in the first half of the W^T buffer (own rows)
+        // fp32 copy for T10; fp16 T tile [t][s]: rows of block I in column p,
+        // and zeros above the diagonal (rows 0-31 of columns 32-63)
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int r0 = 8 * q + 4 * h;
-          const float tv[4] = {col[2 * q].x, col[2 * q].y, col[2 * q + 1].x, col[2 * q + 1].y};
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(r0 + kk, j)) =
-                __float2half_rn(tv[kk]);
+        for (int a = 0; a < 32; ++a) {
+          const float tv = (a & 1) ? col[a / 2].y : col[a / 2].x;
+          Tsc[(32 * I + a) * 32 + cc] = tv;
+          *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(32 * I + a, p)) =
+              __float2half_rn(tv);
+          if (I == 1)
+            *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(a, p)) = __float2half_rn(0.f);
         }
-      }
-      {
+      } else {
         // ---- scaled copies: gQ -> GQ, Kt -> KT, gK in place; 8 loads in flight
         const float* sGam = reinterpret_cast<const float*>(G0 + G_GAM);
         const float* sGamP = reinterpret_cast<const float*>(G0 + G_GAMP);
         const float* sKts = reinterpret_cast<const float*>(G0 + G_KTS);
+        const int pc = p - 64;
 #pragma unroll
         for (int m = 0; m < 2; ++m) {  // m = 0: Q rows (0-63), m = 1: K rows (64-127)
-          uint4 raw[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int rem = p + 128 * u, t = rem >> 4, ch = rem & 15;
-            raw[u] = *reinterpret_cast<const uint4*>(sm + OFF_QK + (ch >> 3) * 16384 +
-                                                     tc::sw128_chunk(64 * m + t, ch & 7));
-          }
+          for (int bt = 0; bt < 2; ++bt) {
+            uint4 raw[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int rem = p + 128 * u, t = rem >> 4, ch = rem & 15;
-            const int half = ch >> 3, cc = ch & 7;
-            if (m == 0) {
-              *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
-                  scale8h(raw[u], __float2half2_rn(sGam[t]));
-            } else {
-              *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
-                  scale8h(raw[u], __float2half2_rn(sKts[t]));
-              *reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 +
-                                        tc::sw128_chunk(64 + t, cc)) =
-                  scale8h(raw[u], __float2half2_rn(sGamP[t]));
+            for (int u = 0; u < 8; ++u) {
+              const int rem = pc + 64 * (8 * bt + u), t = rem >> 4, ch = rem & 15;
+              raw[u] = *reinterpret_cast<const uint4*>(sm + OFF_QK + (ch >> 3) * 16384 +
+                                                       tc::sw128_chunk(64 * m + t, ch & 7));
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int rem = pc + 64 * (8 * bt + u), t = rem >> 4, ch = rem & 15;
+              const int half = ch >> 3, cc = ch & 7;
+              if (m == 0) {
+                *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
+                    scale8h(raw[u], __float2half2_rn(sGam[t]));
+              } else {
+                *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
+                    scale8h(raw[u], __float2half2_rn(sKts[t]));
+                *reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 +
+                                          tc::sw128_chunk(64 + t, cc)) =
+                    scale8h(raw[u], __float2half2_rn(sGamP[t]));
+              }
             }
           }
         }
+      }
+      gsync();
+      {
+        // ---- P = N10 T00 -> sA[32 + a][b] (the slots of N[b][32 + a], above the diagonal)
+        const int a = p >> 2, b0 = (p & 3) * 8;
+        float2 acc[4] = {};
+#pragma unroll 8
+        for (int d = 0; d < 32; ++d) {
+          const float n = sA[d * kAStride + 32 + a];  // N[32 + a][d]
+          const float2 n2 = make_float2(n, n);
+          const float4 t0 = *reinterpret_cast<const float4*>(Tsc + d * 32 + b0);
+          const float4 t1 = *reinterpret_cast<const float4*>(Tsc + d * 32 + b0 + 4);
+          acc[0] = fma2(n2, make_float2(t0.x, t0.y), acc[0]);
+          acc[1] = fma2(n2, make_float2(t0.z, t0.w), acc[1]);
+          acc[2] = fma2(n2, make_float2(t1.x, t1.y), acc[2]);
+          acc[3] = fma2(n2, make_float2(t1.z, t1.w), acc[3]);
+        }
+        float* prow = sA + (32 + a) * kAStride + b0;
+        *reinterpret_cast<float4*>(prow) = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
+        *reinterpret_cast<float4*>(prow + 4) = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
+      }
+      gsync();
+      {
+        // ---- T10 = T11 P -> rows 32-63, columns 0-31 of the T tile
+        const int a = p >> 2, b0 = (p & 3) * 8;
+        float2 acc[4] = {};
+#pragma unroll 8
+        for (int c2 = 0; c2 < 32; ++c2) {
+          const float tv = Tsc[(32 + a) * 32 + c2];  // T11[a][c2]
+          const float2 t2 = make_float2(tv, tv);
+          const float4 p0 = *reinterpret_cast<const float4*>(sA + (32 + c2) * kAStride + b0);
+          const float4 p1 = *reinterpret_cast<const float4*>(sA + (32 + c2) * kAStride + b0 + 4);
+          acc[0] = fma2(t2, make_float2(p0.x, p0.y), acc[0]);
+          acc[1] = fma2(t2, make_float2(p0.z, p0.w), acc[1]);
+          acc[2] = fma2(t2, make_float2(p1.x, p1.y), acc[2]);
+          acc[3] = fma2(t2, make_float2(p1.z, p1.w), acc[3]);
+        }
+        uint4 pk;
+        pk.x = pack2<Op>(acc[0].x, acc[0].y);
+        pk.y = pack2<Op>(acc[1].x, acc[1].y);
+        pk.z = pack2<Op>(acc[2].x, acc[2].y);
+        pk.w = pack2<Op>(acc[3].x, acc[3].y);
+        *reinterpret_cast<uint4*>(sm + OFF_WT + tc::sw128_chunk(32 + a, b0 >> 3)) = pk;
       }
       tc::fence_proxy_async();
       gsync();
