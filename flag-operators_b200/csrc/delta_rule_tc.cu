@@ -323,7 +323,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       }
       // RAW (row-major input dtype) -> fp16 swizzled tiles; rows past the end are
       // zero.  24 chunks of 16 bytes per thread, 8 loads in flight at a time.
-#pragma unroll 1
+#pragma unroll
       for (int base = p; base < 3 * 1024; base += 8 * 128) {
         uint4 val[8];
 #pragma unroll
