@@ -493,7 +493,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         // ---- P = N10 T00 -> sA[32 + a][b] (the slots of N[b][32 + a], above the diagonal)
         const int a = p >> 2, b0 = (p & 3) * 8;
         float2 acc[4] = {};
-#pragma unroll 8
+#pragma unroll
         for (int d = 0; d < 32; ++d) {
           const float n = sA[d * kAStride + 32 + a];  // N[32 + a][d]
           const float2 n2 = make_float2(n, n);
@@ -513,7 +513,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         // ---- T10 = T11 P -> rows 32-63, columns 0-31 of the T tile
         const int a = p >> 2, b0 = (p & 3) * 8;
         float2 acc[4] = {};
-#pragma unroll 8
+#pragma unroll
         for (int c2 = 0; c2 < 32; ++c2) {
           const float tv = Tsc[(32 + a) * 32 + c2];  // T11[a][c2]
           const float2 t2 = make_float2(tv, tv);
