@@ -176,6 +176,13 @@ class Flusher:
         torch.sum(self.rbuf, dim=0, out=self.sink)
 
 
+# GPU-side spin enqueued before each timed step's start event, outside the timed
+# region: while the GPU spins, the host enqueues the whole step, so the events
+# never time a GPU waiting for the host's launches (which happened when several
+# ranks' Python launch paths shared the host cores).  ~0.5 ms at 1.9 GHz.
+_HOST_COVER_CYCLES = 1_000_000
+
+
 def time_steps(fn, steps, warmup, flush=None, dist=None):
     """Sum of per-step CUDA-event times (ms) of `fn`, flush outside the events;
     barrier + synchronize on both sides; max over ranks."""
@@ -191,6 +198,7 @@ def time_steps(fn, steps, warmup, flush=None, dist=None):
     for _ in range(steps):
         if flush:
             flush()
+        torch.cuda._sleep(_HOST_COVER_CYCLES)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
