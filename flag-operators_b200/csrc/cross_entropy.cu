@@ -60,6 +60,22 @@ __device__ __forceinline__ float sum_vec(const float* e) {
   return p[0].x + p[0].y;
 }
 
+// Asks L2 for the 16-byte-aligned interior of [p, p + bytes) with bulk
+// prefetches of at most 32 KiB, one per thread of the first warps: the whole row
+// is requested from DRAM at once instead of as the threads' loads reach it.
+__device__ __forceinline__ void l2_prefetch(const void* p, int64_t bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uintptr_t a0 = (a + 15) & ~(uintptr_t)15;
+  const uintptr_t a1 = (a + (uintptr_t)bytes) & ~(uintptr_t)15;
+  if (a1 <= a0) return;
+  constexpr uintptr_t kPiece = 32768;
+  for (uintptr_t off = (uintptr_t)threadIdx.x * kPiece; a0 + off < a1; off += blockDim.x * kPiece) {
+    const uintptr_t n = (a1 - a0 - off) < kPiece ? (a1 - a0 - off) : kPiece;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a0 + off), "r"((uint32_t)n)
+                 : "memory");
+  }
+}
+
 struct MS {
   float m;  // running max
   float s;  // sum of exp(x - m)
@@ -293,6 +309,7 @@ ce_fwd_kernel(const T* __restrict__ logits, const int64_t* __restrict__ target,
     const bool valid = (t != ignore_index);
     MS st{-INFINITY, 0.f};
     float rsum = 0.f;
+    l2_prefetch(row, V * (int64_t)sizeof(T));
     row_stats<T>(row, V, LS, grad, st, rsum);
     block_ms(st, rsum, sm);
     if (threadIdx.x == 0) {
