@@ -41,8 +41,42 @@ def test_python_signatures_cover_header():
     assert set(_declared()) <= set(_lib.declared_symbols())
 
 
-def test_cpu_tensors_are_rejected_loudly():
+def _cpu_calls():
     import torch
-    from operators.rms_norm import rms_norm
+    from operators.chunk_gated_delta_rule import chunk_gated_delta_rule
+    from operators.fused_cross_entropy import cross_entropy_loss, fused_cross_entropy
+    from operators.median import median
+    from operators.rms_norm import rms_norm, rms_norm_backward, rms_norm_forward, rms_norm_out
+    from operators.scatter_reduce import scatter_reduce, scatter_reduce_, scatter_reduce_out
+    x = torch.randn(4, 8)
+    idx = torch.randint(0, 4, (6,))
+    src, s0 = torch.randn(6), torch.randn(4)
+    tgt = torch.randint(0, 8, (4,))
+    q = torch.randn(1, 1, 8, 16)
+    gate = torch.rand(1, 1, 8)
+    return {
+        "rms_norm": lambda: rms_norm(x, (8,), torch.ones(8)),
+        "rms_norm_forward": lambda: rms_norm_forward(x, (8,), torch.ones(8)),
+        "rms_norm_out": lambda: rms_norm_out(torch.empty(4, 8), x, (8,), torch.ones(8)),
+        "rms_norm_backward": lambda: rms_norm_backward(x, x, torch.ones(4), (8,), torch.ones(8)),
+        "median": lambda: median(x),
+        "median_dim": lambda: median(x, dim=1),
+        "scatter_reduce": lambda: scatter_reduce(s0, 0, idx, src, "sum"),
+        "scatter_reduce_": lambda: scatter_reduce_(s0.clone(), 0, idx, src, "sum"),
+        "scatter_reduce_out": lambda: scatter_reduce_out(torch.empty(4), s0, 0, idx, src, "sum"),
+        "fused_cross_entropy": lambda: fused_cross_entropy(x, tgt),
+        "cross_entropy_loss": lambda: cross_entropy_loss(x, tgt),
+        "chunk_gated_delta_rule": lambda: chunk_gated_delta_rule(q, q, q, gate, gate),
+    }
+
+
+@pytest.mark.parametrize("op", sorted(["rms_norm", "rms_norm_forward", "rms_norm_out",
+                                       "rms_norm_backward", "median", "median_dim",
+                                       "scatter_reduce", "scatter_reduce_", "scatter_reduce_out",
+                                       "fused_cross_entropy", "cross_entropy_loss",
+                                       "chunk_gated_delta_rule"]))
+def test_cpu_tensors_are_rejected_loudly(op):
+    """The product path has no CPU fallback: CPU tensors raise instead of being
+    computed some other way (the reference's CPU branch lives only in oracle/)."""
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
-        rms_norm(torch.randn(4, 8), (8,), torch.ones(8))
+        _cpu_calls()[op]()
