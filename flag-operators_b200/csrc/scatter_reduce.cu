@@ -666,13 +666,19 @@ extern "C" int fo_scatter_reduce_workspace_bytes(int64_t out_numel, int reduce, 
   return FO_OK;
 }
 
-extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, int ndim,
-                                 const int64_t* index_shape, const int64_t* index_strides,
-                                 const int64_t* src_strides, const int64_t* out_shape,
-                                 const int64_t* out_strides, int dim, int reduce,
-                                 int include_self, int dtype, int index_dtype, void* workspace,
-                                 int64_t ws_bytes, int32_t* err_count, void* stream) {
-  clear_error();
+namespace fo {
+namespace {
+inline bool known_dtype(int dt) {
+  return dt == FO_F32 || dt == FO_F16 || dt == FO_BF16 || dt == FO_I32 || dt == FO_I64;
+}
+
+// Argument checks shared by both scatter entry points (same status codes and
+// messages), and the kernel geometry of the call.
+int prepare_scatter(const void* out, const void* src, const void* index, int ndim,
+                    const int64_t* index_shape, const int64_t* index_strides,
+                    const int64_t* src_strides, const int64_t* out_shape,
+                    const int64_t* out_strides, int dim, int reduce, int dtype, int index_dtype,
+                    Geo& g, OutGeo& og, int64_t& n) {
   FO_CHECK_ARG(ndim >= 1 && ndim <= 4, "scatter_reduce supports 1-4-D tensors, got %dD", ndim);
   FO_CHECK_ARG(dim >= 0 && dim < ndim, "scatter_reduce: dim %d out of range", dim);
   FO_CHECK_ARG(reduce >= FO_SUM && reduce <= FO_AMIN, "Unsupported reduce code %d", reduce);
@@ -680,9 +686,13 @@ extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, 
                "scatter_reduce: index must be int64 or int32");
   FO_CHECK_ARG(index_shape && index_strides && src_strides && out_shape && out_strides,
                "scatter_reduce: null shape/stride array");
-  Geo g{};
-  OutGeo og{};
-  int64_t n = 1;
+  if (!known_dtype(dtype)) {
+    set_error("scatter_reduce: unsupported dtype code %d", dtype);
+    return FO_EDTYPE;
+  }
+  g = Geo{};
+  og = OutGeo{};
+  n = 1;
   og.numel = 1;
   for (int d = 0; d < 4; ++d) {
     g.shape[d] = d < ndim ? index_shape[d] : 1;
@@ -692,6 +702,8 @@ extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, 
     og.shape[d] = d < ndim ? out_shape[d] : 1;
     og.str[d] = d < ndim ? out_strides[d] : 0;
     FO_CHECK_ARG(g.shape[d] >= 0 && og.shape[d] >= 0, "scatter_reduce: negative shape");
+    FO_CHECK_ARG(g.istr[d] >= 0 && g.sstr[d] >= 0 && og.str[d] >= 0,
+                 "scatter_reduce: negative stride");
     n *= g.shape[d];
     og.numel *= og.shape[d];
   }
@@ -705,6 +717,25 @@ extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, 
   og.ndim = ndim;
   if (og.numel == 0) return FO_OK;
   FO_CHECK_ARG(out && (n == 0 || (src && index)), "scatter_reduce: null pointer");
+  return FO_OK;
+}
+}  // namespace
+}  // namespace fo
+
+extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, int ndim,
+                                 const int64_t* index_shape, const int64_t* index_strides,
+                                 const int64_t* src_strides, const int64_t* out_shape,
+                                 const int64_t* out_strides, int dim, int reduce,
+                                 int include_self, int dtype, int index_dtype, void* workspace,
+                                 int64_t ws_bytes, int32_t* err_count, void* stream) {
+  clear_error();
+  Geo g;
+  OutGeo og;
+  int64_t n = 0;
+  if (int rc = prepare_scatter(out, src, index, ndim, index_shape, index_strides, src_strides,
+                               out_shape, out_strides, dim, reduce, dtype, index_dtype, g, og, n))
+    return rc;
+  if (og.numel == 0) return FO_OK;
   const int64_t span = out_span(og.shape, og.str, ndim);
   Plan pl = make_plan(reduce, include_self != 0, dtype, span);
   choose_pairs(pl, reduce, include_self != 0, dtype, n);
@@ -738,16 +769,21 @@ extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, 
 
 namespace fo {
 namespace {
-// Accumulator + counts for up to 2^20 output cells (8-byte accumulators
-// included): 12 MiB per device.
+// Accumulator + counts for an output whose memory span (1 + sum over dims of
+// (size - 1) * stride, in elements) is at most 2^20, 8-byte accumulators
+// included: 12 MiB per device.
 constexpr size_t kNoAllocScratchBytes = (size_t)12 << 20;
 __device__ __align__(256) unsigned char g_scatter_scratch[kNoAllocScratchBytes];
 
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[64] = {nullptr};
 
-// Device address of g_scatter_scratch on the current device (looked up once per
-// device; the symbol's name in host code is not a device address).
+// Device address of g_scatter_scratch on the current device, looked up once per
+// device with that device current (the symbol's name in host code is a
+// host-side stand-in, not a device address).  The cached address belongs to the
+// device's primary context: after cudaDeviceReset the library's device code is
+// loaded again and the address may change, so the entry point must not be used
+// after a device reset in the same process.
 int scratch_address(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
@@ -778,16 +814,20 @@ extern "C" int fo_scatter_reduce_noalloc(void* out, const void* src, const void*
                                          int include_self, int dtype, int index_dtype,
                                          int32_t* err_count, void* stream) {
   clear_error();
-  FO_CHECK_ARG(ndim >= 1 && ndim <= 4, "scatter_reduce supports 1-4-D tensors, got %dD", ndim);
-  FO_CHECK_ARG(out_shape && out_strides, "scatter_reduce_noalloc: null shape/stride array");
-  FO_CHECK_ARG(reduce >= FO_SUM && reduce <= FO_AMIN, "Unsupported reduce code %d", reduce);
-  const int64_t span = out_span(out_shape, out_strides, ndim);
+  Geo g;
+  OutGeo og;
+  int64_t n = 0;
+  if (int rc = prepare_scatter(out, src, index, ndim, index_shape, index_strides, src_strides,
+                               out_shape, out_strides, dim, reduce, dtype, index_dtype, g, og, n))
+    return rc;
+  if (og.numel == 0) return FO_OK;
+  const int64_t span = out_span(og.shape, og.str, ndim);
   const Plan pl = make_plan(reduce, include_self != 0, dtype, span);
   const size_t need = pl.acc_bytes + pl.cnt_bytes;
   if (need > kNoAllocScratchBytes) {
     set_error("scatter_reduce_noalloc: this call needs %zu bytes of scratch but the static "
-              "scratch holds %zu (at most 2^20 output cells); use fo_scatter_reduce with a "
-              "caller-provided workspace", need, kNoAllocScratchBytes);
+              "scratch holds %zu (an output memory span of at most 2^20 elements); use "
+              "fo_scatter_reduce with a caller-provided workspace", need, kNoAllocScratchBytes);
     return FO_EWORKSPACE;
   }
   void* ws = nullptr;

@@ -149,12 +149,18 @@ FO_API int fo_scatter_reduce(void* out, const void* src, const void* index, int 
  * whole device heap, a cgo / JNI / plugin caller without the program's
  * allocator, code that must avoid the device synchronisation of cudaMalloc).
  * The scratch is one static 12 MiB device array per device, reserved when the
- * library is loaded and held until the process exits; it covers up to 2^20
- * output cells and larger calls fail with FO_EWORKSPACE.  The first call on a
- * device looks up the array's device address (cudaGetSymbolAddress), so make
- * that first call before any stream capture.  Every call reuses the same array
- * (it is re-initialised per call): calls that overlap on the GPU, from several
- * streams or threads, race and must not be issued.  Allocates nothing.
+ * library is loaded and held until the process exits.  It covers an output
+ * whose memory span (1 + sum over dims of (size - 1) * stride, in elements, so
+ * a strided view counts the whole range it spans, not its cell count) is at
+ * most 2^20; larger calls fail with FO_EWORKSPACE.  Arguments are checked
+ * first, with the same status codes and messages as fo_scatter_reduce.  The
+ * first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and keeps it, so make that first call before any
+ * stream capture, and do not use this entry point after a cudaDeviceReset in
+ * the same process (the kept address may then be stale).  Every call reuses
+ * the same array (it is re-initialised per call): calls that overlap on the
+ * GPU, from several streams or threads, race and must not be issued.
+ * Allocates nothing.
  */
 FO_API int fo_scatter_reduce_noalloc(void* out, const void* src, const void* index, int ndim,
                                      const int64_t* index_shape, const int64_t* index_strides,

@@ -1,6 +1,7 @@
 """Generates tests/golden/*.npz from the reference implementation itself.
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <checkout of the reference>
+    (or FLAGOPS_REFERENCE=<checkout> python tests/golden/make_golden.py)
 
 Imports the reference's operators.* modules (iamsuperfly/Flag-Operators) and
 runs their public functions on CPU tensors, i.e. the reference's CPU branch,
@@ -45,8 +46,11 @@ def _save(name: str, **tensors):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("FLAGOPS_REFERENCE"),
+                    help="checkout of iamsuperfly/Flag-Operators (or set FLAGOPS_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or FLAGOPS_REFERENCE")
     sys.path.insert(0, args.ref)
     from operators.rms_norm import rms_norm_forward            # reference module
     from operators.median import median

@@ -88,9 +88,16 @@ def test_vocab_sharded_cross_entropy_two_gpus():
     procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
-    out = [q.get(timeout=300) for _ in procs]
-    for p in procs:
-        p.join(timeout=60)
+    try:
+        out = [q.get(timeout=300) for _ in procs]
+    finally:
+        # never leave a rank holding a GPU: join, then end any rank still alive
+        for p in procs:
+            p.join(timeout=60)
+        for p in procs:
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
     for rank, res in out:
         assert isinstance(res, list), f"rank {rank}: {res}"
         assert not res, f"rank {rank} mismatches: {res}"

@@ -52,6 +52,14 @@ def _no_alloc(self_, src, index, reduce, include_self, dim=0):
     return out
 
 
+def _no_alloc_view(out, src, index, reduce, include_self, dim=0):
+    """In place on `out`, keeping its strides (a view of a larger tensor)."""
+    _lib.call("fo_scatter_reduce_noalloc", *_args(out, src, index, dim), _CODE[reduce],
+              int(include_self), _lib.dtype_code(out.dtype), _lib.dtype_code(index.dtype), None,
+              _lib.stream_of(out))
+    return out
+
+
 def _inputs(seed, n_self=1 << 16, n_src=1 << 20):
     g = torch.Generator().manual_seed(seed)
     self_ = torch.randn(n_self, generator=g)
@@ -110,3 +118,32 @@ def test_no_alloc_rejects_sizes_beyond_the_static_scratch():
     # a reduce that needs no scratch has no limit
     out = _no_alloc(self_, src, index, "sum", True)
     assert out[0].item() == 16.0
+
+
+def test_no_alloc_limit_is_the_output_memory_span():
+    # a column of a [2^19, 4] matrix has 2^19 cells but spans 2^21 - 3 elements
+    base = torch.zeros(1 << 19, 4, device=DEV)
+    col = base[:, 0]
+    src = torch.ones(16, device=DEV)
+    index = torch.arange(16, device=DEV)
+    with pytest.raises(RuntimeError, match="memory span"):
+        _no_alloc_view(col, src, index, "mean", False)
+    # the same cells stored contiguously fit
+    out = _no_alloc(col.contiguous(), src, index, "mean", False)
+    assert out[:16].eq(1.0).all()
+
+
+def test_no_alloc_argument_errors_match_the_workspace_entry_point():
+    src = torch.ones(16, device=DEV)
+    index = torch.zeros(16, dtype=torch.int64, device=DEV)
+    out = torch.zeros(64, device=DEV)
+    bad_shape = _lib.i64_array([-5])
+    args = (_lib.ptr(out), _lib.ptr(src), _lib.ptr(index), 1, _lib.i64_array(index.shape),
+            _lib.i64_array(index.stride()), _lib.i64_array(src.stride()), bad_shape,
+            _lib.i64_array(out.stride()), 0, _CODE["mean"], 0, _lib.dtype_code(out.dtype),
+            _lib.dtype_code(index.dtype))
+    with pytest.raises(ValueError, match="negative shape") as e1:
+        _lib.call("fo_scatter_reduce_noalloc", *args, None, _lib.stream_of(out))
+    with pytest.raises(ValueError, match="negative shape") as e2:
+        _lib.call("fo_scatter_reduce", *args, None, 0, None, _lib.stream_of(out))
+    assert str(e1.value) == str(e2.value)
