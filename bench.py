@@ -17,8 +17,11 @@ the delta rule), each with its own roofline and CPU baseline.
 oracle, i.e. the reference's torch CPU branch) on the host cores for the same
 workload and metric.  Multi-GPU: one process per GPU; each rank runs the full
 per-GPU workload (weak scaling, no collective on the data path); time = max over
-ranks.  With N > 1 a vocabulary-sharded cross-entropy line (NCCL all-gather of
-row statistics) is added to per_op.
+ranks.  With N > 1, per_op also holds each workload split over the ranks
+(strong scaling): rms_norm and median rows, cross-entropy rows (two one-float
+all-reduces) and vocabulary columns (all-gather of row statistics), delta-rule
+heads; each of those lines checks its rank's shard against the oracle and
+reports `parity` ("ok" or "FAIL ..."); a failure makes the exit status 1.
 """
 from __future__ import annotations
 
@@ -300,11 +303,21 @@ def torch_threads():
     return torch.get_num_threads()
 
 
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_entry(fn, nbytes_or_units, unit, sample, kind="port", per="GB/s"):
     t = cpu_time(fn)
     val = nbytes_or_units / t / (1e9 if per == "GB/s" else 1.0)
     return {"value": round(val, 4), "unit": unit, "cores": torch.get_num_threads(), "kind": kind,
-            "sample": sample}
+            "cpu": cpu_model(), "sample": sample}
 
 
 def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
@@ -450,26 +463,6 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
              "effective_GBps_3pass": round(3 * B * V * 2 / (ms / K / 1e3) / 1e9, 1)})
         del ld, td, logits
 
-    # vocabulary-sharded cross-entropy (N > 1): each rank holds V / N columns
-    if want("ce_vocab_sharded") or only is None:
-        if dist is not None and dist.get_world_size() > 1:
-            P, rank = dist.get_world_size(), dist.get_rank()
-            Vn = V // P
-            lg, tg = ce_inputs()
-            lsh = lg[:, rank * Vn:(rank + 1) * Vn].contiguous().to(dev)
-            tgd = tg.to(dev)
-
-            def ce_sh():
-                x = lsh.detach().requires_grad_(True)
-                fused_cross_entropy(x, tgd, process_group=dist.group.WORLD, vocab_size=Vn * P).backward()
-
-            ms = time_steps(ce_sh, K, W, flush, dist)
-            nb = 3 * B * Vn * 2
-            e = hbm_entry("ce_vocab_sharded", nb * P, ms, K, 5, hbm * P, src, traffic, None,
-                          {"scaling": "strong", "ranks": P, "collective": "all_gather of [B,4] fp32"})
-            res["ce_vocab_sharded"] = e
-            del lsh, lg
-
     # delta rule
     if want("chunk_gated_delta_rule"):
         ins = delta_inputs()
@@ -486,17 +479,211 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
                   "tensor": {"achieved_tflops": round(flops / t / 1e12, 2), "peak_tflops": tfl,
                              "frac": round(flops / t / 1e12 / tfl, 4), "algorithmic_flops": flops}})
         if do_cpu:
-            Ls = 256
-            sub_in = [x[:, :, :Ls] if x.dim() == 3 else x[:, :, :Ls, :] for x in ins]
-            sub_in = [x[:1, :2].contiguous() for x in sub_in]
+            # the L=512 prefix of all B x H heads; the recurrence is linear in L
+            Ls = 512
+            sub_in = [(x[:, :, :Ls] if x.dim() == 3 else x[:, :, :Ls, :]).contiguous()
+                      for x in ins]
             tc = cpu_time(lambda: oracle.delta_rule_forward(*sub_in, output_final_state=True),
                           min_reps=2, min_seconds=0.5)
-            # tokens/s of the full 8x16 heads extrapolated linearly from 1x2 heads, L=256
-            full_t = tc * (Bd * Hd) / 2 * (Ld / Ls)
+            full_t = tc * (Ld / Ls)
             e["cpu_baseline"] = {"value": round(Bd * Ld / full_t, 3), "unit": "tokens/s",
                                  "cores": torch.get_num_threads(), "kind": "port",
-                                 "sample": f"B=1 H=2 L={Ls}, scaled linearly to B=8 H=16 L=8192"}
+                                 "cpu": cpu_model(),
+                                 "sample": f"all {Bd}x{Hd} heads, L={Ls} prefix, scaled "
+                                           f"linearly to L={Ld}"}
         res["chunk_gated_delta_rule"] = e
+    return res
+
+
+# ---------------------------------------------------------------------------
+# strong-scaled splits over the ranks (N > 1), each with a parity check
+# ---------------------------------------------------------------------------
+def _bounds(n, rank, world):
+    return rank * n // world, (rank + 1) * n // world
+
+
+def _agree(dist, ok, detail):
+    """'ok' when every rank passed, else 'FAIL <first failing rank's detail>'."""
+    t = torch.tensor([0.0 if ok else 1.0], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if t.item() == 0.0:
+        return "ok"
+    return "FAIL " + (detail or "on another rank")
+
+
+def _delta_close(got, ref, rtol=2e-2):
+    got, ref = got.float().cpu(), ref.float().cpu()
+    rms = ref.pow(2).mean().sqrt().item()
+    err = (got - ref).abs()
+    ok = bool((err <= rtol * ref.abs() + rtol * rms).all())
+    return ok, f"max err {err.max().item():.3e} (rms {rms:.3e})"
+
+
+def run_sharded(args, dev, peaks, traffic, dist):
+    """Each workload of the target spec split over the ranks (strong scaling):
+    rms_norm and median rows, cross-entropy rows and vocabulary columns, delta
+    rule heads.  value = bytes (tokens) of the whole workload / max-over-ranks
+    time.  Every line checks its rank's shard against the oracle and reports
+    `parity`; a failure makes bench.py exit non-zero."""
+    import oracle
+    from operators.median import median
+    from operators.rms_norm import rms_norm_forward
+    from operators.fused_cross_entropy import fused_cross_entropy
+    from operators.chunk_gated_delta_rule import chunk_gated_delta_rule
+    hbm, tfl, src = peaks
+    P, rank = dist.get_world_size(), dist.get_rank()
+    flush = Flusher(dev)
+    K, W = args.steps, max(3, args.warmup)
+    only = getattr(args, "only", None)
+    res = {}
+
+    def want(name):
+        return only is None or name.startswith(only) or only.startswith(name)
+
+    def line(name, nbytes, ms, launches, parity, extra=None):
+        e = hbm_entry(name, nbytes, ms, K, launches, hbm * P, src, traffic)
+        e.update({"scaling": "strong", "ranks": P, "parity": parity})
+        if extra:
+            e.update(extra)
+        return e
+
+    if want("rms_norm_bf16_rows"):
+        x, w = rms_inputs("bf16")
+        M, N = x.shape
+        r0, r1 = _bounds(M, rank, P)
+        xd, wd = x[r0:r1].contiguous().to(dev), w.to(dev)
+        ms = time_steps(lambda: rms_norm_forward(xd, (N,), wd, 1e-6), K, W, flush, dist)
+        y, _ = rms_norm_forward(xd, (N,), wd, 1e-6)
+        rows = torch.arange(0, r1 - r0, 61)
+        yr, _ = oracle.rms_norm_forward(x[r0:r1][rows], (N,), w, 1e-6)
+        ok = bool(torch.allclose(y[rows.to(dev)].float().cpu(), yr.float(), rtol=2e-2, atol=2e-2))
+        res["rms_norm_bf16_rows"] = line(
+            "rms_norm_bf16_rows", rms_bytes(x), ms, 1,
+            _agree(dist, ok, f"rank {rank} rms_norm rows"),
+            {"shard": f"rows [{r0}, {r1}) of {M} on rank {rank} (each rank M/N rows)"})
+        del xd, wd, y
+
+    if want("median_a_rows"):
+        x = median_inputs("a")
+        M = x.shape[0]
+        r0, r1 = _bounds(M, rank, P)
+        xd = x[r0:r1].contiguous().to(dev)
+        ms = time_steps(lambda: median(xd, dim=-1), K, W, flush, dist)
+        got = median(xd, dim=-1)
+        ref = oracle.median(x[r0:r1], dim=-1)
+        ok = (torch.equal(got.values.cpu(), ref.values)
+              and torch.equal(got.indices.cpu(), ref.indices))
+        res["median_a_rows"] = line(
+            "median_a_rows", median_bytes(x), ms, 1,
+            _agree(dist, ok, f"rank {rank} median rows not bit-exact"),
+            {"shard": f"rows [{r0}, {r1}) of {M} (each rank M/N rows)"})
+        del xd
+
+    if want("ce_rows_sharded") or want("ce_vocab_sharded"):
+        lg, tg = ce_inputs()
+        B, V = lg.shape
+        tgd = tg.to(dev)
+        nbytes = 2 * B * V * lg.element_size()       # one read + one write of B x V
+        sample = torch.arange(0, B, 97)
+        n_valid = int((tg != -100).sum())
+        # oracle: full-batch loss on rank 0 (fp32 upcast), gradient rows sampled
+        ref_loss = None
+        if rank == 0:
+            ref_loss = float(oracle.fused_cross_entropy(lg.float(), tg))
+        _, gs = oracle.fused_cross_entropy_grad(lg[sample].float(), tg[sample], reduction="sum")
+        gs = gs / n_valid
+
+        def loss_ok(loss):
+            t = torch.tensor([float(loss)], device=dev, dtype=torch.float64)
+            lo, hi = t.clone(), t.clone()
+            dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+            dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+            same = lo.item() == hi.item()
+            if rank == 0:
+                return same and abs(float(loss) - ref_loss) <= 2e-2 * abs(ref_loss), \
+                    f"loss {float(loss):.6f} vs oracle {ref_loss:.6f}, ranks agree: {same}"
+            return same, "ranks disagree on the loss"
+
+        if want("ce_rows_sharded"):
+            r0, r1 = _bounds(B, rank, P)
+            lsh = lg[r0:r1].contiguous().to(dev)
+            td = tgd[r0:r1].contiguous()
+
+            def ce_rows():
+                x = lsh.detach().requires_grad_(True)
+                loss = fused_cross_entropy(x, td, process_group=dist.group.WORLD, shard="rows")
+                loss.backward()
+                return loss, x.grad
+
+            ms = time_steps(lambda: ce_rows(), K, W, flush, dist)
+            loss, grad = ce_rows()
+            ok, det = loss_ok(loss.float().item())
+            mine = sample[(sample >= r0) & (sample < r1)]
+            if ok and mine.numel():
+                ok = bool(torch.allclose(grad[(mine - r0).to(dev)].float().cpu(),
+                                         gs[(sample >= r0) & (sample < r1)], rtol=2e-2,
+                                         atol=2e-5 * float(gs.abs().max())))
+                det = det if ok else f"rank {rank} gradient rows differ"
+            res["ce_rows_sharded"] = line(
+                "ce_rows_sharded", nbytes, ms, 4, _agree(dist, ok, det),
+                {"shard": f"rows [{r0}, {r1}) of {B}, full vocabulary",
+                 "collective": "all_reduce of the valid-row count, then of the loss sum (fp32)"})
+            del lsh, grad
+
+        if want("ce_vocab_sharded"):
+            c0, c1 = _bounds(V, rank, P)
+            lsh = lg[:, c0:c1].contiguous().to(dev)
+
+            def ce_sh():
+                x = lsh.detach().requires_grad_(True)
+                loss = fused_cross_entropy(x, tgd, process_group=dist.group.WORLD,
+                                           vocab_offset=c0, vocab_size=V)
+                loss.backward()
+                return loss, x.grad
+
+            ms = time_steps(lambda: ce_sh(), K, W, flush, dist)
+            loss, grad = ce_sh()
+            ok, det = loss_ok(loss.float().item())
+            if ok:
+                ok = bool(torch.allclose(grad[sample.to(dev)].float().cpu(), gs[:, c0:c1],
+                                         rtol=2e-2, atol=2e-5 * float(gs.abs().max())))
+                det = det if ok else f"rank {rank} gradient block differs"
+            res["ce_vocab_sharded"] = line(
+                "ce_vocab_sharded", nbytes, ms, 5, _agree(dist, ok, det),
+                {"shard": f"columns [{c0}, {c1}) of {V}, all rows",
+                 "collective": "all_gather of per-row (max, sum-exp, target logit, row sum)",
+                 "note": "algorithmic bytes = one read of the logits + one write of dlogits"})
+            del lsh, grad
+        del lg
+
+    if want("delta_heads"):
+        ins = delta_inputs()
+        Bd, Hd, Ld, Dd = ins[0].shape
+        nh = Bd * Hd
+        h0, h1 = _bounds(nh, rank, P)
+
+        def heads(t):
+            return t.reshape(1, nh, *t.shape[2:])[:, h0:h1].contiguous()
+
+        dins = [heads(t).to(dev) for t in ins]
+        ms = time_steps(lambda: chunk_gated_delta_rule(*dins, output_final_state=True), K, W,
+                        flush, dist)
+        o, hT = chunk_gated_delta_rule(*dins, output_final_state=True)
+        ro, rh = oracle.delta_rule_forward(*[heads(t)[:, :1] for t in ins],
+                                           output_final_state=True)
+        ok1, d1 = _delta_close(o[:, :1], ro)
+        ok2, d2 = _delta_close(hT[:, :1], rh)
+        t = ms / K / 1e3
+        e = line("delta_heads", delta_bytes(), ms, 1,
+                 _agree(dist, ok1 and ok2, f"rank {rank} head {h0}: o {d1}; state {d2}"),
+                 {"shard": f"heads [{h0}, {h1}) of B*H = {nh} (each rank B*H/N heads)"})
+        e.update({"metric": "chunk_gated_delta_rule tokens/s (heads split over ranks)",
+                  "value": round(Bd * Ld / t, 1), "unit": "tokens/s (B*L per second)",
+                  "tensor": {"achieved_tflops": round(delta_flops() / t / 1e12, 2),
+                             "peak_tflops": tfl * P,
+                             "frac": round(delta_flops() / t / 1e12 / (tfl * P), 4)}})
+        res["delta_heads"] = e
+        del dins
     return res
 
 
@@ -548,6 +735,7 @@ def main():
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, spec shapes)",
             "config": workload,
             "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": n, "kind": "port",
+                             "cpu": cpu_model(),
                              "sample": "full workload per step (torch CPU median, the "
                                        "reference's CPU branch)"},
             "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -575,13 +763,15 @@ def main():
     if args.only:
         do_cpu = (rank == 0 and world == 1)
         per_op = run_per_op(args, dev, peaks, traffic, do_cpu, dist)
+        if dist is not None:
+            per_op.update(run_sharded(args, dev, peaks, traffic, dist))
         clocks = sampler.stop()
         if rank == 0:
             print(json.dumps({"only": args.only, "per_op": per_op, "clocks": clocks}))
         if dist is not None:
             dist.barrier()
             dist.destroy_process_group()
-        return
+        return 1 if _parity_failed(per_op) else 0
 
     # ---- headline: median (a), device-resident
     x = median_inputs("a")
@@ -618,6 +808,8 @@ def main():
         cpu = cpu_entry(lambda: oracle.median(x, dim=-1), nbytes, "GB/s",
                         "full workload (torch CPU median, the reference's CPU branch)")
     per_op = {} if args.no_per_op else run_per_op(args, dev, peaks, traffic, do_cpu, dist)
+    if dist is not None and not args.no_per_op:
+        per_op.update(run_sharded(args, dev, peaks, traffic, dist))
     clocks = sampler.stop()
 
     if rank == 0:
@@ -643,7 +835,16 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    return 1 if _parity_failed(per_op) else 0
+
+
+def _parity_failed(per_op):
+    bad = {k: v["parity"] for k, v in per_op.items()
+           if str(v.get("parity", "ok")).startswith("FAIL")}
+    if bad:
+        sys.stderr.write(f"parity failures: {bad}\n")
+    return bool(bad)
 
 
 if __name__ == "__main__":
-    main()
+    sys.exit(main())

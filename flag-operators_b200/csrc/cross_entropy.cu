@@ -688,3 +688,59 @@ extern "C" int fo_ce_shard_bwd(const void* logits, const int64_t* target, const 
                                      label_smoothing, reduction, st);
   }
 }
+
+// Row-sharded cross-entropy: this rank holds rows of the batch; n_valid_global
+// (device fp32, the number of non-ignored rows over every rank, already summed
+// by the caller) scales the fused gradient for 'mean'.  local_sum_out (device
+// fp32, nullable for 'none') receives the sum of this rank's row losses; the
+// caller sums it over ranks and divides by n_valid_global for 'mean'.
+extern "C" int fo_ce_rows_fwd(const void* logits, const int64_t* target, float* loss_rows,
+                              float* lse, float* local_sum_out, const float* n_valid_global,
+                              void* dlogits, int64_t B, int64_t V, int64_t ld,
+                              int64_t ignore_index, float label_smoothing, int reduction,
+                              int dtype, void* stream) {
+  clear_error();
+  if (int rc = check_common(logits, target, B, V, ld, dtype, "fo_ce_rows_fwd")) return rc;
+  FO_CHECK_ARG(reduction >= FO_RED_NONE && reduction <= FO_RED_SUM,
+               "fo_ce_rows_fwd: bad reduction %d", reduction);
+  FO_CHECK_ARG(n_valid_global && (B == 0 || (loss_rows && lse)),
+               "fo_ce_rows_fwd: null pointer");
+  FO_CHECK_ARG(reduction == FO_RED_NONE || local_sum_out, "fo_ce_rows_fwd: null local_sum_out");
+  FO_CHECK_ARG(label_smoothing >= 0.f && label_smoothing <= 1.f,
+               "fo_ce_rows_fwd: bad label_smoothing");
+  cudaStream_t st = as_stream(stream);
+  if (B > 0) {
+    const int grid = grid_rows(B, dlogits ? 2 : 4);
+#define FO_ROWS_FWD(T)                                                                         \
+  if (label_smoothing != 0.f)                                                                  \
+    ce_fwd_kernel<T, true><<<grid, kThreads, 0, st>>>((const T*)logits, target, loss_rows, lse, \
+                                                      (T*)dlogits, n_valid_global, B, V, ld,   \
+                                                      ignore_index, label_smoothing, reduction); \
+  else                                                                                         \
+    ce_fwd_kernel<T, false><<<grid, kThreads, 0, st>>>((const T*)logits, target, loss_rows,    \
+                                                       lse, (T*)dlogits, n_valid_global, B, V, \
+                                                       ld, ignore_index, label_smoothing,      \
+                                                       reduction)
+    switch (dtype) {
+      case FO_F32: FO_ROWS_FWD(float); break;
+      case FO_F16: FO_ROWS_FWD(__half); break;
+      default: FO_ROWS_FWD(__nv_bfloat16); break;
+    }
+#undef FO_ROWS_FWD
+    if (int rc = check_launch("ce_fwd_kernel")) return rc;
+  }
+  if (reduction != FO_RED_NONE) {
+    ce_reduce_kernel<<<1, 1024, 0, st>>>(loss_rows, B, n_valid_global, FO_RED_SUM, local_sum_out);
+    return check_launch("ce_reduce_kernel");
+  }
+  return FO_OK;
+}
+
+// n_valid_out[0] (device fp32) = number of target entries != ignore_index.
+extern "C" int fo_ce_count_valid(const int64_t* target, int64_t B, int64_t ignore_index,
+                                 float* n_valid_out, void* stream) {
+  clear_error();
+  FO_CHECK_ARG(B >= 0 && n_valid_out && (B == 0 || target), "fo_ce_count_valid: bad argument");
+  ce_count_valid_kernel<<<1, 1024, 0, as_stream(stream)>>>(target, B, ignore_index, n_valid_out);
+  return check_launch("ce_count_valid_kernel");
+}

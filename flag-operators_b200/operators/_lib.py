@@ -63,6 +63,8 @@ _SIGS = {
     "fo_ce_shard_bwd": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _int, _int, _c_void_p,
                         _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _int, _int,
                         _c_void_p],
+    "fo_ce_count_valid": [_c_void_p, _i64, _i64, _c_void_p, _c_void_p],
+    "fo_ce_rows_fwd": [_c_void_p] * 7 + [_i64, _i64, _i64, _i64, _f32, _int, _int, _c_void_p],
     "fo_gdr_fwd": [_c_void_p] * 8 + [_i64, _i64, _i64, _i64, _int, _int, _c_void_p],
     "fo_gdr_fwd_stepwise": [_c_void_p] * 8 + [_i64, _i64, _i64, _i64, _int, _int, _c_void_p],
     "fo_gdr_timeouts": [_c_void_p],

@@ -16,6 +16,9 @@ Extension (keyword-only, default keeps the reference behaviour):
 ``process_group=`` computes the loss of vocabulary-sharded logits: each rank
 holds columns [rank*V_local, (rank+1)*V_local) of the [B, V] logits; per-row
 (max, sum-exp, target logit, row sum) are all-gathered over NCCL and combined.
+``shard="rows"`` instead splits the batch rows over the ranks: the fused
+one-read/one-write kernel runs unchanged on each rank's rows, and 'mean' adds two
+one-float all-reduces (the valid-row count before the kernel, the loss sum after).
 """
 from __future__ import annotations
 
@@ -111,7 +114,8 @@ class _ShardedCrossEntropy(torch.autograd.Function):
         _lib.call("fo_ce_shard_stats", _lib.ptr(logits), _lib.ptr(target), _lib.ptr(stats), B,
                   Vn, ld, v_offset, int(ignore_index), _lib.dtype_code(logits.dtype),
                   _lib.stream_of(logits))
-        all_stats = torch.empty(P, B, 4, dtype=torch.float32, device=dev)
+        # [P * B, 4]: rank p's rows at [p * B, (p + 1) * B) (the layout NCCL and gloo share)
+        all_stats = torch.empty(P * B, 4, dtype=torch.float32, device=dev)
         dist.all_gather_into_tensor(all_stats, stats, group=group)
         loss_rows = torch.empty(B, dtype=torch.float32, device=dev)
         lse = torch.empty(B, dtype=torch.float32, device=dev)
@@ -141,6 +145,60 @@ class _ShardedCrossEntropy(torch.autograd.Function):
         return dlogits, None, None, None, None, None, None, None
 
 
+class _RowShardedCrossEntropy(torch.autograd.Function):
+    """Cross-entropy over a row block of the batch on each rank.
+
+    'mean' needs the batch-wide count of non-ignored rows before the fused
+    gradient is written (one all-reduce of a float) and the batch-wide loss sum
+    after it (a second all-reduce of a float); 'sum' only the second; 'none'
+    no collective at all.
+    """
+
+    @staticmethod
+    def forward(ctx, logits, target, reduction, ignore_index, label_smoothing, group):
+        import torch.distributed as dist
+        B, V = logits.shape
+        dev = logits.device
+        target = target.to(torch.int64).contiguous()
+        if logits.stride(1) != 1:
+            logits = logits.contiguous()
+        ld = logits.stride(0) if B > 1 else V
+        st = _lib.stream_of(logits)
+        n_valid = torch.empty(1, dtype=torch.float32, device=dev)
+        _lib.call("fo_ce_count_valid", _lib.ptr(target), B, int(ignore_index), _lib.ptr(n_valid),
+                  st)
+        if reduction == "mean":
+            dist.all_reduce(n_valid, group=group)
+        loss_rows = torch.empty(B, dtype=torch.float32, device=dev)
+        lse = torch.empty(B, dtype=torch.float32, device=dev)
+        local_sum = torch.empty(1, dtype=torch.float32, device=dev)
+        want_grad = bool(ctx.needs_input_grad[0])
+        dlogits = torch.empty((B, V), dtype=logits.dtype, device=dev) if want_grad else None
+        _lib.call("fo_ce_rows_fwd", _lib.ptr(logits), _lib.ptr(target), _lib.ptr(loss_rows),
+                  _lib.ptr(lse), _lib.ptr(local_sum), _lib.ptr(n_valid), _lib.ptr(dlogits), B, V,
+                  ld, int(ignore_index), float(label_smoothing), _RED[reduction],
+                  _lib.dtype_code(logits.dtype), st)
+        if reduction == "none":
+            out = loss_rows
+        else:
+            dist.all_reduce(local_sum, group=group)
+            out = (local_sum / n_valid if reduction == "mean" else local_sum).reshape(())
+        ctx.reduction = reduction
+        ctx.ignore_index = int(ignore_index)
+        ctx.label_smoothing = float(label_smoothing)
+        ctx.B, ctx.V, ctx.ld = B, V, ld
+        ctx.grad_ready = dlogits is not None
+        if dlogits is not None:
+            ctx.save_for_backward(logits, target, lse, n_valid, dlogits)
+        else:
+            ctx.save_for_backward(logits, target, lse, n_valid)
+        return out.to(logits.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        return _FusedCrossEntropy.backward(ctx, grad_output) + (None,)
+
+
 def shard_layout(rank: int, world: int, v_local: int, vocab_offset=None, vocab_size=None):
     """(first global column of this rank's block, full vocabulary size).
 
@@ -164,19 +222,31 @@ def fused_cross_entropy(
     process_group=None,
     vocab_offset: int | None = None,
     vocab_size: int | None = None,
+    shard: str = "vocab",
 ) -> torch.Tensor:
     """Fused cross-entropy (fused_cross_entropy.py:302-357).
 
     logits [B, V], target [B] int64; reduction 'none' | 'mean' | 'sum'.
-    With process_group, logits is this rank's [B, V_local] column block; the
-    block starts at vocab_offset (default rank * V_local) of a vocabulary of
-    vocab_size columns (default V_local * world_size).
+    With process_group and shard='vocab' (default), logits is this rank's
+    [B, V_local] column block; the block starts at vocab_offset (default
+    rank * V_local) of a vocabulary of vocab_size columns (default
+    V_local * world_size).  With shard='rows', logits [B_local, V] and target
+    [B_local] are this rank's rows of the batch: 'none' returns this rank's row
+    losses, 'sum' and 'mean' the loss of the whole batch on every rank (mean
+    over the non-ignored rows of all ranks), and the gradient of this rank's rows.
     """
     logger.debug("FLAG-OPS FUSED_CROSS_ENTROPY")
     _check(logits, target, reduction)
     _lib.require_cuda(logits, "fused_cross_entropy")
     if not 0.0 <= float(label_smoothing) <= 1.0:
         raise ValueError(f"label_smoothing must be in [0, 1], got {label_smoothing}")
+    if process_group is not None and shard == "rows":
+        if vocab_offset is not None or vocab_size is not None:
+            raise ValueError("vocab_offset / vocab_size apply to shard='vocab' only")
+        return _RowShardedCrossEntropy.apply(logits, target, reduction, ignore_index,
+                                             label_smoothing, process_group)
+    if shard not in ("vocab", "rows"):
+        raise ValueError(f"shard must be 'vocab' or 'rows', got {shard!r}")
     if process_group is not None:
         import torch.distributed as dist
         off, V = shard_layout(dist.get_rank(process_group), dist.get_world_size(process_group),

@@ -247,6 +247,26 @@ FO_API int fo_ce_shard_bwd(const void* logits, const int64_t* target, const floa
                     int64_t ignore_index, float label_smoothing, int reduction,
                     int dtype, void* stream);
 
+/*
+ * Row-sharded cross-entropy: each rank holds a block of rows [B_local, V] of
+ * the batch.  fo_ce_count_valid counts this rank's non-ignored targets; the
+ * caller sums the counts over ranks (one all-reduce) and passes the total as
+ * n_valid_global.  fo_ce_rows_fwd then writes per-row loss and lse, the
+ * gradient for grad_output == 1 (dlogits nullable; scaled by 1/n_valid_global
+ * for FO_RED_MEAN) and local_sum_out[0] = sum of this rank's row losses, which
+ * the caller sums over ranks (second all-reduce) and divides by n_valid_global
+ * for 'mean'.  The backward for other grad_output values is fo_ce_bwd with
+ * n_valid = n_valid_global.  Partitions the rows of
+ * operators/fused_cross_entropy.py:302-357 (no counterpart in the reference).
+ */
+FO_API int fo_ce_count_valid(const int64_t* target, int64_t B, int64_t ignore_index,
+                             float* n_valid_out, void* stream);
+FO_API int fo_ce_rows_fwd(const void* logits, const int64_t* target, float* loss_rows,
+                          float* lse, float* local_sum_out, const float* n_valid_global,
+                          void* dlogits, int64_t B, int64_t V, int64_t ld,
+                          int64_t ignore_index, float label_smoothing, int reduction,
+                          int dtype, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* chunk_gated_delta_rule                                                    */
 /* ------------------------------------------------------------------------ */

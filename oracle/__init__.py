@@ -26,4 +26,6 @@ from .ops import (  # noqa: F401
     delta_rule_forward,
     ce_shard_stats,
     ce_shard_combine,
+    ce_rows_partial,
+    ce_rows_combine,
 )

@@ -216,3 +216,21 @@ def ce_shard_combine(all_stats, target, V, ignore_index=-100, label_smoothing=0.
     if reduction == "sum":
         return loss.sum()
     return loss.sum() / valid.sum()
+
+
+# ---------------------------------------------------------------------------
+# row-sharded cross-entropy: each rank holds a block of the batch's rows; the
+# single-device result it must reproduce is F.cross_entropy above
+# ---------------------------------------------------------------------------
+def ce_rows_partial(logits_rows, target_rows, ignore_index=-100, label_smoothing=0.0):
+    """(sum of this block's row losses, number of non-ignored rows), float64."""
+    loss = F.cross_entropy(_cpu(logits_rows).double(), _cpu(target_rows), reduction="none",
+                           ignore_index=ignore_index, label_smoothing=label_smoothing)
+    n = (_cpu(target_rows) != ignore_index).sum()
+    return torch.stack([loss.sum(), n.double()])
+
+
+def ce_rows_combine(partials, reduction="mean"):
+    """Combines the [P, 2] per-rank (loss sum, valid rows) into the batch loss."""
+    tot = _cpu(partials).double().sum(dim=0)
+    return tot[0] / tot[1] if reduction == "mean" else tot[0]

@@ -73,6 +73,55 @@ def test_vocab_sharded_ce_two_ranks_gloo(uneven):
             assert err < 1e-4, (rank, k, err)
 
 
+def _rows_worker(rank, world, port, bounds, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        g = torch.Generator().manual_seed(9)
+        B, V = bounds[-1], 777
+        logits = torch.randn(B, V, generator=g) * 2
+        target = torch.randint(0, V, (B,), generator=g)
+        target[::5] = -100
+        lo, hi = bounds[rank], bounds[rank + 1]
+        res = {}
+        for ls in (0.0, 0.1):
+            part = oracle.ce_rows_partial(logits[lo:hi], target[lo:hi], label_smoothing=ls)
+            parts = [torch.empty_like(part) for _ in range(world)]
+            dist.all_gather(parts, part)
+            for red in ("mean", "sum"):
+                got = oracle.ce_rows_combine(torch.stack(parts), red)
+                ref = oracle.fused_cross_entropy(logits.double(), target, reduction=red,
+                                                 label_smoothing=ls)
+                res[(red, ls)] = float((got - ref).abs())
+        q.put((rank, res))
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("bounds", [[0, 20, 40], [0, 7, 40]])
+def test_row_sharded_ce_two_ranks_gloo(bounds):
+    """Row blocks (even and uneven): the per-rank (loss sum, valid rows) pairs
+    summed over ranks give the single-device 'mean' and 'sum' losses."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rows_worker, args=(r, 2, port, bounds, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        out = [q.get(timeout=120) for _ in procs]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+    for rank, res in out:
+        assert isinstance(res, dict), f"rank {rank} failed: {res}"
+        for k, err in res.items():
+            assert err < 1e-9, (rank, k, err)
+
+
 def test_shard_layout_rules():
     assert shard_layout(1, 4, 100) == (100, 400)
     assert shard_layout(0, 2, 30, vocab_offset=0, vocab_size=50) == (0, 50)

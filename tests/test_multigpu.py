@@ -1,4 +1,4 @@
-"""Vocabulary-sharded fused_cross_entropy on 2 GPUs (one process per GPU, NCCL).
+"""Vocabulary- and row-sharded fused_cross_entropy on 2 GPUs (one process per GPU, NCCL).
 
 Each rank holds a column block of the logits; the loss and this rank's block of
 the gradient must equal the single-device result of the oracle on the whole
@@ -72,6 +72,17 @@ def _worker(rank, port, q):
                     ok_g = _close(x.grad.cpu(), rg[:, lo:hi].to(dtype), dtype)
                     if not (ok_l and ok_g):
                         fails.append((B, V, str(dtype), split, red, ls, ok_l, ok_g))
+                    # the same batch split by rows instead
+                    r0, r1 = rank * B // WORLD, (rank + 1) * B // WORLD
+                    xr = logits[r0:r1].contiguous().to(dev).requires_grad_(True)
+                    lr = fused_cross_entropy(xr, target[r0:r1].to(dev), reduction=red,
+                                             label_smoothing=ls, process_group=dist.group.WORLD,
+                                             shard="rows")
+                    lr.backward(torch.ones_like(lr))
+                    want = rl[r0:r1] if red == "none" else rl
+                    if not (_close(lr.detach().cpu(), want.to(dtype), dtype)
+                            and _close(xr.grad.cpu(), rg[r0:r1].to(dtype), dtype)):
+                        fails.append(("rows", B, V, str(dtype), red, ls))
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, fails))
