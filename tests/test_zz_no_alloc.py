@@ -146,4 +146,5 @@ def test_no_alloc_argument_errors_match_the_workspace_entry_point():
         _lib.call("fo_scatter_reduce_noalloc", *args, None, _lib.stream_of(out))
     with pytest.raises(ValueError, match="negative shape") as e2:
         _lib.call("fo_scatter_reduce", *args, None, 0, None, _lib.stream_of(out))
-    assert str(e1.value) == str(e2.value)
+    # same status and message; only the entry point's name in front differs
+    assert str(e1.value).split(": ", 1)[1] == str(e2.value).split(": ", 1)[1]
