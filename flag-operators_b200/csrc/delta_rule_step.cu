@@ -21,7 +21,11 @@ template <typename T, typename G, int D>
 __global__ void __launch_bounds__(kStepThreads)
 gdr_step_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                 const G* __restrict__ beta, const G* __restrict__ g, const float* __restrict__ h0,
-                T* __restrict__ o, float* __restrict__ hT, int64_t L) {
+                T* __restrict__ o, float* __restrict__ hT, const int* __restrict__ only,
+                int64_t L) {
+  // with `only`, heads whose entry is 0 are left alone (recomputation of the
+  // heads the tensor-core kernel marked)
+  if (only && only[blockIdx.x] == 0) return;
   constexpr int TPR = kStepThreads / D;  // threads per state row
   constexpr int CPT = D / TPR;           // columns per thread
   __shared__ float s_k[2][D], s_q[2][D], s_v[2][D], s_bg[2][2];
@@ -79,11 +83,11 @@ gdr_step_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 
 template <typename T, typename G>
 int launch_step(const void* q, const void* k, const void* v, const void* beta, const void* g,
-                const float* h0, void* o, float* hT, int64_t BH, int64_t L, int64_t D,
-                cudaStream_t st) {
+                const float* h0, void* o, float* hT, const int* only, int64_t BH, int64_t L,
+                int64_t D, cudaStream_t st) {
 #define FO_STEP(DD)                                                                          \
   gdr_step_kernel<T, G, DD><<<(unsigned)BH, kStepThreads, 0, st>>>(                          \
-      (const T*)q, (const T*)k, (const T*)v, (const G*)beta, (const G*)g, h0, (T*)o, hT, L)
+      (const T*)q, (const T*)k, (const T*)v, (const G*)beta, (const G*)g, h0, (T*)o, hT, only, L)
   switch (D) {
     case 16: FO_STEP(16); break;
     case 32: FO_STEP(32); break;
@@ -100,11 +104,12 @@ int launch_step(const void* q, const void* k, const void* v, const void* beta, c
 template <typename T>
 int step_gate_dispatch(int gate_dtype, const void* q, const void* k, const void* v,
                        const void* beta, const void* g, const float* h0, void* o, float* hT,
-                       int64_t BH, int64_t L, int64_t D, cudaStream_t st) {
+                       const int* only, int64_t BH, int64_t L, int64_t D, cudaStream_t st) {
   switch (gate_dtype) {
-    case FO_F32: return launch_step<T, float>(q, k, v, beta, g, h0, o, hT, BH, L, D, st);
-    case FO_F16: return launch_step<T, __half>(q, k, v, beta, g, h0, o, hT, BH, L, D, st);
-    case FO_BF16: return launch_step<T, __nv_bfloat16>(q, k, v, beta, g, h0, o, hT, BH, L, D, st);
+    case FO_F32: return launch_step<T, float>(q, k, v, beta, g, h0, o, hT, only, BH, L, D, st);
+    case FO_F16: return launch_step<T, __half>(q, k, v, beta, g, h0, o, hT, only, BH, L, D, st);
+    case FO_BF16:
+      return launch_step<T, __nv_bfloat16>(q, k, v, beta, g, h0, o, hT, only, BH, L, D, st);
   }
   set_error("chunk_gated_delta_rule: unsupported gate dtype code %d", gate_dtype);
   return FO_EDTYPE;
@@ -114,13 +119,17 @@ int step_gate_dispatch(int gate_dtype, const void* q, const void* k, const void*
 
 int gdr_stepwise(const void* q, const void* k, const void* v, const void* beta, const void* g,
                  const float* h0, void* o, float* hT, int64_t B, int64_t H, int64_t L, int64_t D,
-                 int dtype, int gate_dtype, cudaStream_t st) {
+                 int dtype, int gate_dtype, cudaStream_t st, const int* only) {
   const int64_t BH = B * H;
   switch (dtype) {
-    case FO_F32: return step_gate_dispatch<float>(gate_dtype, q, k, v, beta, g, h0, o, hT, BH, L, D, st);
-    case FO_F16: return step_gate_dispatch<__half>(gate_dtype, q, k, v, beta, g, h0, o, hT, BH, L, D, st);
+    case FO_F32:
+      return step_gate_dispatch<float>(gate_dtype, q, k, v, beta, g, h0, o, hT, only, BH, L, D, st);
+    case FO_F16:
+      return step_gate_dispatch<__half>(gate_dtype, q, k, v, beta, g, h0, o, hT, only, BH, L, D,
+                                        st);
     case FO_BF16:
-      return step_gate_dispatch<__nv_bfloat16>(gate_dtype, q, k, v, beta, g, h0, o, hT, BH, L, D, st);
+      return step_gate_dispatch<__nv_bfloat16>(gate_dtype, q, k, v, beta, g, h0, o, hT, only, BH,
+                                               L, D, st);
   }
   set_error("chunk_gated_delta_rule: unsupported dtype code %d", dtype);
   return FO_EDTYPE;
@@ -145,5 +154,5 @@ extern "C" int fo_gdr_fwd_stepwise(const void* q, const void* k, const void* v, 
     return FO_OK;
   }
   return fo::gdr_stepwise(q, k, v, beta, g, h0, o, hT, B, H, L, D, dtype, gate_dtype,
-                          fo::as_stream(stream));
+                          fo::as_stream(stream), nullptr);
 }

@@ -42,7 +42,7 @@
 namespace fo {
 int gdr_stepwise(const void* q, const void* k, const void* v, const void* beta, const void* g,
                  const float* h0, void* o, float* hT, int64_t B, int64_t H, int64_t L, int64_t D,
-                 int dtype, int gate_dtype, cudaStream_t st);
+                 int dtype, int gate_dtype, cudaStream_t st, const int* only = nullptr);
 
 __device__ unsigned int g_gdr_timeouts;
 
@@ -169,7 +169,7 @@ template <typename T, typename G>
 __global__ void __launch_bounds__(kThr, 1)
 gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
               const G* __restrict__ beta, const G* __restrict__ g, const float* __restrict__ h0,
-              T* __restrict__ o, float* __restrict__ hT, int64_t L) {
+              T* __restrict__ o, float* __restrict__ hT, int* __restrict__ flags, int64_t L) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~(uintptr_t)1023);
@@ -250,6 +250,12 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
     return any != 0;
   };
   auto gtab = [&](int b) { return sm + OFF_G + b * kGateBytes; };
+  // fp16 range guard.  An operand that leaves the fp16 range becomes inf, and
+  // an inf reaches every later output through the products (as inf or NaN,
+  // 0 * inf included), so the chain group watches what it writes: the fp32
+  // outputs o and the final state.  nf = sum of 0 * x stays 0 while every x is
+  // finite and turns NaN at the first non-finite one (one FMA per value).
+  float nf = 0.f;
 
   if (!is_chain) {
     // =====================================================================
@@ -723,7 +729,11 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
           tc::tmem_ld32(tm_lane + TM_O + 32 * hf, r);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) so[(32 * hf + j) * kD + i] = from_f<T>(__uint_as_float(r[j]));
+          for (int j = 0; j < 32; ++j) {
+            const float x = __uint_as_float(r[j]);
+            nf = fmaf(0.f, x, nf);
+            so[(32 * hf + j) * kD + i] = from_f<T>(x);
+          }
         }
 #pragma unroll
         for (int hq = 0; hq < 4; ++hq) {
@@ -767,14 +777,21 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
           for (int j = 0; j < 32; ++j) r[j] = 0u;
         }
 #pragma unroll
+        for (int j = 0; j < 32; ++j) nf = fmaf(0.f, __uint_as_float(r[j]), nf);
+#pragma unroll
         for (int j4 = 0; j4 < 8; ++j4)
           *reinterpret_cast<uint4*>(hh + i * kD + 32 * hq + 4 * j4) =
               make_uint4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
       }
     }
   }
+  // a head with a non-finite output (an fp16 operand overflowed, or the inputs
+  // were not finite) or that gave up on a wait is marked for recomputation by
+  // the fp32 per-step kernel
+  const int bad = (nf != nf) || *reinterpret_cast<volatile int*>(s_abort);
   tc::fence_before_sync();
-  __syncthreads();
+  const int any_bad = __syncthreads_or(bad);
+  if (tid == 0 && flags) flags[head] = any_bad;
   if (warp == 0) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tm, TM_COLS);
@@ -783,7 +800,8 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
 
 template <typename T, typename G>
 int launch_tc(const void* q, const void* k, const void* v, const void* beta, const void* g,
-              const float* h0, void* o, float* hT, int64_t BH, int64_t L, cudaStream_t st) {
+              const float* h0, void* o, float* hT, int* flags, int64_t BH, int64_t L,
+              cudaStream_t st) {
   auto kern = gdr_tc_kernel<T, G>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
       cudaSuccess) {
@@ -791,18 +809,20 @@ int launch_tc(const void* q, const void* k, const void* v, const void* beta, con
     return FO_ECUDA;
   }
   kern<<<(unsigned)BH, kThr, kSmemBytes, st>>>((const T*)q, (const T*)k, (const T*)v,
-                                               (const G*)beta, (const G*)g, h0, (T*)o, hT, L);
+                                               (const G*)beta, (const G*)g, h0, (T*)o, hT, flags,
+                                               L);
   return check_launch("gdr_tc_kernel");
 }
 
 template <typename T>
 int tc_gate_dispatch(int gate_dtype, const void* q, const void* k, const void* v, const void* beta,
-                     const void* g, const float* h0, void* o, float* hT, int64_t BH, int64_t L,
-                     cudaStream_t st) {
+                     const void* g, const float* h0, void* o, float* hT, int* flags, int64_t BH,
+                     int64_t L, cudaStream_t st) {
   switch (gate_dtype) {
-    case FO_F32: return launch_tc<T, float>(q, k, v, beta, g, h0, o, hT, BH, L, st);
-    case FO_F16: return launch_tc<T, __half>(q, k, v, beta, g, h0, o, hT, BH, L, st);
-    case FO_BF16: return launch_tc<T, __nv_bfloat16>(q, k, v, beta, g, h0, o, hT, BH, L, st);
+    case FO_F32: return launch_tc<T, float>(q, k, v, beta, g, h0, o, hT, flags, BH, L, st);
+    case FO_F16: return launch_tc<T, __half>(q, k, v, beta, g, h0, o, hT, flags, BH, L, st);
+    case FO_BF16:
+      return launch_tc<T, __nv_bfloat16>(q, k, v, beta, g, h0, o, hT, flags, BH, L, st);
   }
   set_error("chunk_gated_delta_rule: unsupported gate dtype code %d", gate_dtype);
   return FO_EDTYPE;
@@ -895,9 +915,27 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const __nv_bfloat16* _
 
 using namespace fo;
 
+namespace {
+inline bool gdr_tc_eligible(const void* q, const void* k, const void* v, const void* o,
+                            const float* hT, int64_t D, int dtype) {
+  return D == 128 && (dtype == FO_BF16 || dtype == FO_F16) && aligned16(q) && aligned16(k) &&
+         aligned16(v) && aligned16(o) && (!hT || aligned16(hT));
+}
+}  // namespace
+
+extern "C" int fo_gdr_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t D, int dtype,
+                                      int64_t* bytes) {
+  clear_error();
+  FO_CHECK_ARG(bytes && B >= 0 && H >= 0 && L >= 0, "fo_gdr_workspace_bytes: bad argument");
+  // the tensor-core path keeps one int flag per head (fp16 range guard)
+  *bytes = (D == 128 && (dtype == FO_BF16 || dtype == FO_F16)) ? B * H * (int64_t)sizeof(int) : 0;
+  return FO_OK;
+}
+
 extern "C" int fo_gdr_fwd(const void* q, const void* k, const void* v, const void* beta,
                           const void* g, const float* h0, void* o, float* hT, int64_t B, int64_t H,
-                          int64_t L, int64_t D, int dtype, int gate_dtype, void* stream) {
+                          int64_t L, int64_t D, int dtype, int gate_dtype, void* workspace,
+                          int64_t ws_bytes, void* stream) {
   clear_error();
   FO_CHECK_ARG(B >= 0 && H >= 0 && L >= 0, "chunk_gated_delta_rule: negative size");
   if (D != 16 && D != 32 && D != 64 && D != 128) {
@@ -906,6 +944,8 @@ extern "C" int fo_gdr_fwd(const void* q, const void* k, const void* v, const voi
   }
   if (B * H == 0) return FO_OK;
   FO_CHECK_ARG(q && k && v && beta && g && o, "chunk_gated_delta_rule: null pointer");
+  FO_CHECK_ARG(!(h0 && hT && (const void*)h0 == (const void*)hT),
+               "chunk_gated_delta_rule: initial and final state must not alias");
   cudaStream_t st = as_stream(stream);
   if (L == 0) {
     if (hT && h0)
@@ -914,12 +954,22 @@ extern "C" int fo_gdr_fwd(const void* q, const void* k, const void* v, const voi
       cudaMemsetAsync(hT, 0, B * H * D * D * sizeof(float), st);
     return FO_OK;
   }
-  const bool tc_ok = D == 128 && (dtype == FO_BF16 || dtype == FO_F16) && aligned16(q) &&
-                     aligned16(k) && aligned16(v) && aligned16(o) && (!hT || aligned16(hT));
-  if (tc_ok) {
-    if (dtype == FO_BF16)
-      return tc_gate_dispatch<__nv_bfloat16>(gate_dtype, q, k, v, beta, g, h0, o, hT, B * H, L, st);
-    return tc_gate_dispatch<__half>(gate_dtype, q, k, v, beta, g, h0, o, hT, B * H, L, st);
+  if (gdr_tc_eligible(q, k, v, o, hT, D, dtype)) {
+    const int64_t need = B * H * (int64_t)sizeof(int);
+    if (!workspace || ws_bytes < need) {
+      set_error("chunk_gated_delta_rule: workspace of %lld bytes required, got %lld",
+                (long long)need, (long long)ws_bytes);
+      return FO_EWORKSPACE;
+    }
+    int* flags = reinterpret_cast<int*>(workspace);
+    int rc = dtype == FO_BF16 ? tc_gate_dispatch<__nv_bfloat16>(gate_dtype, q, k, v, beta, g, h0,
+                                                                o, hT, flags, B * H, L, st)
+                              : tc_gate_dispatch<__half>(gate_dtype, q, k, v, beta, g, h0, o, hT,
+                                                         flags, B * H, L, st);
+    if (rc) return rc;
+    // heads whose fp16 operands left the fp16 range: exact fp32 per-step recomputation
+    // (every other head's CTA returns at once)
+    return gdr_stepwise(q, k, v, beta, g, h0, o, hT, B, H, L, D, dtype, gate_dtype, st, flags);
   }
   return gdr_stepwise(q, k, v, beta, g, h0, o, hT, B, H, L, D, dtype, gate_dtype, st);
 }

@@ -65,7 +65,9 @@ _SIGS = {
                         _c_void_p],
     "fo_ce_count_valid": [_c_void_p, _i64, _i64, _c_void_p, _c_void_p],
     "fo_ce_rows_fwd": [_c_void_p] * 7 + [_i64, _i64, _i64, _i64, _f32, _int, _int, _c_void_p],
-    "fo_gdr_fwd": [_c_void_p] * 8 + [_i64, _i64, _i64, _i64, _int, _int, _c_void_p],
+    "fo_gdr_workspace_bytes": [_i64, _i64, _i64, _i64, _int, _i64p],
+    "fo_gdr_fwd": [_c_void_p] * 8 + [_i64, _i64, _i64, _i64, _int, _int, _c_void_p, _i64,
+                                     _c_void_p],
     "fo_gdr_fwd_stepwise": [_c_void_p] * 8 + [_i64, _i64, _i64, _i64, _int, _int, _c_void_p],
     "fo_gdr_timeouts": [_c_void_p],
     "fo_median_timeouts": [_c_void_p],

@@ -11,12 +11,15 @@ Keyword-only extensions (defaults keep the reference behaviour):
 
 Kernels: D = 128 with bf16/fp16 inputs runs the chunked tensor-core kernel
 (csrc/delta_rule_tc.cu: chunks of 64 tokens, seven tcgen05 GEMMs per chunk,
-fp32 state in TMEM); other shapes run the per-step kernel
+fp32 state in TMEM, fp16 operand tiles); a head whose fp16 operands would leave
+the fp16 range is recomputed in the same call by the fp32 per-step kernel, so
+finite inputs give finite outputs.  Other shapes run the per-step kernel
 (csrc/delta_rule_step.cu).  _ref_forward is kept importable, as the reference's
 tests import it; it is the reference's sequential fp32 loop on CPU tensors.
 """
 from __future__ import annotations
 
+import ctypes
 import logging
 
 import torch
@@ -65,9 +68,13 @@ def chunk_gated_delta_rule(
         h0 = initial_state.to(device=q.device, dtype=torch.float32).contiguous()
     hT = torch.empty(B, H, D, D, dtype=torch.float32, device=q.device) \
         if output_final_state else None
+    nbytes = ctypes.c_int64(0)
+    _lib.call("fo_gdr_workspace_bytes", B, H, L, D, _lib.dtype_code(q.dtype),
+              ctypes.byref(nbytes))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device) if nbytes.value else None
     _lib.call("fo_gdr_fwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(beta), _lib.ptr(g),
               _lib.ptr(h0), _lib.ptr(o), _lib.ptr(hT), B, H, L, D, _lib.dtype_code(q.dtype),
-              _lib.dtype_code(beta.dtype), _lib.stream_of(q))
+              _lib.dtype_code(beta.dtype), _lib.ptr(ws), nbytes.value, _lib.stream_of(q))
     if output_final_state:
         return o, hT
     return o

@@ -274,15 +274,22 @@ FO_API int fo_ce_rows_fwd(const void* logits, const int64_t* target, float* loss
  * h_t = g_t h_{t-1} + beta_t (v_t - h_{t-1} k_t) k_t^T,  o_t = h_t q_t
  * q, k, v, o: [B, H, L, D] contiguous (dtype); beta, g: [B, H, L] (gate_dtype);
  * h0: [B, H, D, D] fp32 initial state or NULL (zeros); hT: [B, H, D, D] fp32
- * final state or NULL.  D in {16, 32, 64, 128}.  D = 128 with bf16/fp16 runs
- * the chunked tcgen05 kernel; the other cases run the per-step kernel.
+ * final state or NULL (h0 and hT must not alias).  D in {16, 32, 64, 128}.
+ * D = 128 with bf16/fp16 runs the chunked tcgen05 kernel, whose operands are
+ * fp16 tiles: a head whose fp16 operands would leave the fp16 range (|x| >=
+ * 65504, e.g. bf16 inputs of 1e5) is marked in the workspace (one int per head,
+ * fo_gdr_workspace_bytes) and recomputed by the fp32 per-step kernel in the
+ * same call, so finite inputs never turn into inf/NaN.  The other cases run
+ * the per-step kernel and need no workspace.
  * Replaces chunk_gated_delta_rule, operators/chunk_gated_delta_rule.py:208-268
  * (kernels chunk_gated_delta_rule.py:71-191).
  */
+FO_API int fo_gdr_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t D, int dtype,
+                                  int64_t* bytes);
 FO_API int fo_gdr_fwd(const void* q, const void* k, const void* v, const void* beta,
                const void* g, const float* h0, void* o, float* hT, int64_t B,
                int64_t H, int64_t L, int64_t D, int dtype, int gate_dtype,
-               void* stream);
+               void* workspace, int64_t ws_bytes, void* stream);
 /* Same recurrence, always through the per-step CUDA-core kernel (any D in
  * {16,32,64,128}); kept as an independent on-device cross-check. */
 FO_API int fo_gdr_fwd_stepwise(const void* q, const void* k, const void* v,

@@ -123,9 +123,9 @@ def test_cross_entropy_argument_checks():
 
 def test_delta_rule_checks():
     with pytest.raises(RuntimeError, match="D=100"):
-        _lib.call("fo_gdr_fwd", *([None] * 8), 1, 1, 16, 100, BF16, BF16, None)
+        _lib.call("fo_gdr_fwd", *([None] * 8), 1, 1, 16, 100, BF16, BF16, None, 0, None)
     with pytest.raises(ValueError, match="negative size"):
-        _lib.call("fo_gdr_fwd", *([None] * 8), -1, 1, 16, 128, BF16, BF16, None)
-    _lib.call("fo_gdr_fwd", *([None] * 8), 0, 4, 16, 128, BF16, BF16, None)  # no heads
+        _lib.call("fo_gdr_fwd", *([None] * 8), -1, 1, 16, 128, BF16, BF16, None, 0, None)
+    _lib.call("fo_gdr_fwd", *([None] * 8), 0, 4, 16, 128, BF16, BF16, None, 0, None)  # no heads
     with pytest.raises(ValueError, match="N, K in"):
         _lib.call("fo_tc05_selftest", DUMMY, DUMMY, DUMMY, 32, 64, 0, 0, None)

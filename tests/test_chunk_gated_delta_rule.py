@@ -150,6 +150,61 @@ def test_gate_edge_cases(case):
     _close(got, oracle.delta_rule_forward(q, k, v, beta, g))
 
 
+def _flags_of(ins):
+    """Runs the C ABI directly and returns (o, hT, per-head range flags)."""
+    import ctypes
+    dins = [t.to(DEV) for t in ins]
+    B, H, L, D = dins[0].shape
+    o = torch.empty_like(dins[0])
+    hT = torch.empty(B, H, D, D, device=DEV)
+    n = ctypes.c_int64(0)
+    _lib.call("fo_gdr_workspace_bytes", B, H, L, D, _lib.dtype_code(dins[0].dtype),
+              ctypes.byref(n))
+    ws = torch.full((n.value // 4,), -1, dtype=torch.int32, device=DEV)
+    _lib.call("fo_gdr_fwd", *[_lib.ptr(t) for t in dins], None, _lib.ptr(o), _lib.ptr(hT),
+              B, H, L, D, _lib.dtype_code(dins[0].dtype), _lib.dtype_code(dins[3].dtype),
+              _lib.ptr(ws), n.value, _lib.stream_of(o))
+    return o, hT, ws.cpu()
+
+
+@pytest.mark.parametrize("case", ["v_1e5", "q_1e5", "persistent_gates"])
+def test_fp16_range_guard(case):
+    """bf16 inputs whose values, or whose state, leave the fp16 range of the
+    tensor-core operand tiles: the result still matches the fp32 recurrence and
+    is finite.  Head 0 holds the large values; head 1 is ordinary and must stay
+    on the tensor-core path (its range flag stays 0)."""
+    L = 2048
+    q, k, v, beta, g = [t.float() for t in _make(1, 2, L, 128, torch.bfloat16, seed=11)]
+    if case == "v_1e5":
+        v[:, 0] *= 1e5
+    elif case == "q_1e5":
+        q[:, 0] *= 1e5
+    else:
+        g[:, 0] = 0.9999
+        beta[:, 0] = 1.0
+        v[:, 0] *= 3e3
+    ins = [t.bfloat16() for t in (q, k, v, beta, g)]
+    o, hT, flags = _flags_of(ins)
+    ref_o, ref_h = oracle.delta_rule_forward(*ins, output_final_state=True)
+    assert bool(torch.isfinite(o).all()) and bool(torch.isfinite(hT).all())
+    for hh in range(2):
+        _close(o[:, hh], ref_o[:, hh])
+        _close(hT[:, hh], ref_h[:, hh])
+    assert flags[1].item() == 0, "an ordinary head left the tensor-core path"
+    assert flags[0].item() in (0, 1)
+
+
+def test_fp16_range_guard_flags_only_the_overflowing_head():
+    q, k, v, beta, g = [t.float() for t in _make(1, 3, 256, 128, torch.bfloat16, seed=12)]
+    v[:, 1] *= 1e5
+    ins = [t.bfloat16() for t in (q, k, v, beta, g)]
+    o, hT, flags = _flags_of(ins)
+    assert flags.tolist() == [0, 1, 0]
+    ref_o, ref_h = oracle.delta_rule_forward(*ins, output_final_state=True)
+    _close(o, ref_o)
+    _close(hT, ref_h)
+
+
 @pytest.mark.parametrize("D", [16, 32, 64, 128])
 @pytest.mark.parametrize("L", [8, 64, 256])
 def test_stepwise_path_fp32(D, L):
