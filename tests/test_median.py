@@ -13,8 +13,8 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def _exact(x_cpu, dim=-1, keepdim=False):
-    got = median(x_cpu.to(DEV), dim=dim, keepdim=keepdim)
+def _exact(x_cpu, dim=-1, keepdim=False, x_dev=None):
+    got = median(x_cpu.to(DEV) if x_dev is None else x_dev, dim=dim, keepdim=keepdim)
     ref = oracle.median(x_cpu, dim=dim, keepdim=keepdim)
     assert got.values.shape == ref.values.shape and got.indices.shape == ref.indices.shape
     assert torch.equal(got.indices.cpu(), ref.indices), "indices differ"
@@ -169,6 +169,54 @@ def test_int32_full_rows(N):
     x[2] = 2**31 - 1
     x[3:10] = torch.randint(-3, 3, (7, N), generator=g).to(torch.int32)
     _exact(x)
+
+
+def _sweep_rows(N, g):
+    """Rows that exercise the special paths of the row kernels."""
+    x = torch.randn(24, N, generator=g)
+    x[1] = torch.randint(-4, 4, (N,), generator=g).float()             # wide ties
+    x[2] = torch.where(torch.rand(N, generator=g) < 0.5, torch.tensor(-0.0),
+                       torch.tensor(0.0))                               # zeros of both signs
+    x[3, ::3] = 0.0
+    x[3, 1::3] = -0.0                                                    # zero median, mixed signs
+    x[4] = 1.0 + torch.rand(N, generator=g) * 1e-4                       # one top-bit bin
+    x[5] = torch.randn(N, generator=g) * 1e-39                           # subnormals around 0
+    x[6, N // 3] = float("nan")
+    x[7, : N // 2 + 1] = float("inf")
+    x[8, ::2] = float("-inf")
+    x[9] = torch.where(torch.rand(N, generator=g) < 0.5, torch.tensor(0.0),
+                       torch.tensor(1e-42))                              # +0 beside subnormals
+    x[10] = torch.where(torch.rand(N, generator=g) < 0.5, torch.tensor(-0.0),
+                        torch.tensor(-1e-42))                            # -0 beside subnormals
+    x[11] = -torch.arange(N).float()
+    return x
+
+
+@pytest.mark.parametrize("layout", ["vector", "scalar"])
+def test_row_length_sweep(layout):
+    """Row lengths 1..2048 in steps that cross every row-group size of the row
+    kernels (full and partial groups), 16-byte and scalar loads (rows starting
+    4 bytes past a 16-byte boundary), fp32 and int32, with ties, signed zeros,
+    subnormals, NaN and infinities."""
+    g = torch.Generator().manual_seed(77)
+    if layout == "vector":
+        lengths = sorted({4 * i for i in range(1, 513, 9)} | {128 * e for e in range(1, 17)})
+    else:
+        lengths = sorted(set(range(1, 2049, 23)) | {32 * e + 1 for e in range(0, 64)})
+    for N in lengths:
+        x = _sweep_rows(N, g)
+        xi = torch.randint(-2**31, 2**31 - 1, (8, N), generator=g, dtype=torch.int64)
+        xi[1] = torch.randint(-3, 3, (N,), generator=g)
+        xi = xi.to(torch.int32)
+        if layout == "scalar" and N % 4 == 0:
+            # contiguous rows starting 4 bytes past a 16-byte boundary: scalar loads
+            for t in (x, xi):
+                buf = torch.zeros(t.numel() + 1, dtype=t.dtype, device=DEV)
+                buf[1:] = t.reshape(-1).to(DEV)
+                _exact(t, x_dev=buf[1:].view(t.shape))
+        else:
+            _exact(x)
+            _exact(xi)
 
 
 def test_no_handoff_timeouts():
