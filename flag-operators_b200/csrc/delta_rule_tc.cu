@@ -34,6 +34,7 @@
 // fp32 state never leaves TMEM between chunks (its bf16 copy in shared memory is
 // the operand of (d)/(e)).  The 64x64 triangular inverse is a blocked forward
 // substitution in fp32 on the CUDA cores.  One CTA per (batch, head).
+#include <cuda.h>
 #include <math.h>
 
 #include "common.cuh"
@@ -56,16 +57,16 @@ constexpr uint32_t kWaitLimit = 1u << 22;
 // shared-memory map (bytes from a 1024-aligned base).  Owner: P = prep warps,
 // C = chain warps, P->C = written by prep, read by the chain (single buffer,
 // guarded by the chain's MMA-completion barriers).
-constexpr uint32_t OFF_QK = 0;         // P    2 x [128 x 128B]: rows 0-63 Q, 64-127 K (then gK)
-constexpr uint32_t OFF_V = 32768;      // P    2 x [64 x 128B]   V
+constexpr uint32_t OFF_QK = 0;         // P    2 x [128 x 128B]: rows 0-63 Q, 64-127 K (then gK)  tile set 0
+constexpr uint32_t OFF_V = 32768;      // P    2 x [64 x 128B]   V                               tile set 0
 constexpr uint32_t OFF_GQ = 49152;     // P->C 2 x [64 x 128B]   gQ
 constexpr uint32_t OFF_KT = 65536;     // P->C 2 x [64 x 128B]   Kt
-constexpr uint32_t OFF_WT = 81920;     // P->C [128 x 128B]      -W^T (T [64 x 128B] before it)
+constexpr uint32_t OFF_WT = 81920;     // P->C [128 x 128B]      -W^T
 constexpr uint32_t OFF_P = 98304;      // C    [64 x 128B]       P
 constexpr uint32_t OFF_S = 106496;     // C    2 x [128 x 128B]  state (fp16 copy)
 constexpr uint32_t OFF_UT = 139264;    // C    [128 x 128B]      U^T; then output staging [64 x 256B]
-constexpr uint32_t OFF_RAW = 155648;   // P    [3][64 x 256B]    q, k, v rows of the next chunk
-constexpr uint32_t OFF_A = 204800;     // P    fp32 [64][68]     A (rows 16-byte aligned)
+constexpr uint32_t OFF_SET1 = 155648;  // P    tile set 1: QK at +0, V at +32768 (48 KB)
+constexpr uint32_t OFF_T = 204800;     // P    2 x [64 x 128B]   T = (I + A)^-1 (gdr_tinv_kernel)
 constexpr uint32_t OFF_G = 222208;     // gate tables x 2 (P->C), then barriers
 constexpr int kAStride = 68;
 constexpr uint32_t kGateBytes = 2304;
@@ -159,23 +160,20 @@ struct GateTabs {
   }
 };
 
-__device__ __forceinline__ void cta_sync_tc() {
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-}
-
 template <typename T, typename G>
 __global__ void __launch_bounds__(kThr, 1)
 gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
               const G* __restrict__ beta, const G* __restrict__ g, const float* __restrict__ h0,
-              T* __restrict__ o, float* __restrict__ hT, int* __restrict__ flags, int64_t L) {
+              T* __restrict__ o, float* __restrict__ hT, int* __restrict__ flags,
+              const __half* __restrict__ tin, const __grid_constant__ CUtensorMap tmq,
+              const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+              int64_t L) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~(uintptr_t)1023);
   const uint32_t sb = tc::smem_u32(sm);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* bar_raw = bars + 0;    // bulk copy of a chunk landed            (prep)
+  // bars[0], bars[7]: tile set 0 / 1 loaded (prep)
   uint64_t* bar_pmma = bars + 1;   // prep's MMAs completed                  (prep)
   uint64_t* bar_prep = bars + 2;   // prep products of a chunk ready         (prep -> chain)
   uint64_t* bar_b1 = bars + 3;     // chain MMAs (d),(e) completed           (chain -> both)
@@ -183,7 +181,6 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   uint64_t* bar_done = bars + 5;   // [2] chain finished a chunk (per buffer) (chain -> prep)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 64);
   int* s_abort = reinterpret_cast<int*>(sm + OFF_BAR + 68);
-  float* sA = reinterpret_cast<float*>(sm + OFF_A);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool is_chain = warp < 4;
@@ -206,7 +203,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int b = 0; b < 7; ++b) tc::mbar_init(bars + b, 1);
+    for (int b = 0; b < 8; ++b) tc::mbar_init(bars + b, 1);
     tc::fence_mbar_init();
     *s_abort = 0;
   }
@@ -262,22 +259,37 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
     // prep warps: everything of a chunk that does not need the state
     // =====================================================================
     const int p = gt_id;
-    uint32_t raw_phase = 0, pmma_phase = 0;
-    auto issue_raw = [&](int64_t c) {
-      const int64_t t0 = c * kC;
-      const int nv = (int)((L - t0) < kC ? (L - t0) : kC);
-      const uint32_t bytes = (uint32_t)nv * kD * sizeof(T);
-      tc::mbar_arrive_expect_tx(bar_raw, 3 * bytes);
-      tc::bulk_g2s(sm + OFF_RAW, qh + t0 * kD, bytes, bar_raw);
-      tc::bulk_g2s(sm + OFF_RAW + 16384, kh + t0 * kD, bytes, bar_raw);
-      tc::bulk_g2s(sm + OFF_RAW + 32768, vh + t0 * kD, bytes, bar_raw);
+    uint32_t pmma_phase = 0;
+    // Chunk c's q, k, v tiles land by TMA (bf16/fp16, 128-byte swizzled, rows
+    // past the head's end zero-filled) in tile set c & 1, together with its T
+    // tile; chunk c + 1's loads are issued when chunk c starts, so they have a
+    // whole chunk to arrive.
+    static_assert(OFF_V == OFF_QK + 32768, "a tile set is QK then V");
+    auto set_base = [&](int64_t c) -> uint32_t { return (c & 1) ? OFF_SET1 : OFF_QK; };
+    auto ld_bar = [&](int64_t c) -> uint64_t* { return (c & 1) ? bars + 7 : bars + 0; };
+    int64_t issued = -1, landed = -1;
+    auto issue_load = [&](int64_t c) {
+      const uint32_t base = set_base(c);
+      uint64_t* bar = ld_bar(c);
+      tc::mbar_arrive_expect_tx(bar, 6 * 8192 + 8192);
+      const int t0 = (int)(c * kC), hz = (int)head;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        tc::tma_load_3d(sm + base + h * 16384, &tmq, 64 * h, t0, hz, bar);
+        tc::tma_load_3d(sm + base + h * 16384 + 8192, &tmk, 64 * h, t0, hz, bar);
+        tc::tma_load_3d(sm + base + 32768 + h * 8192, &tmv, 64 * h, t0, hz, bar);
+      }
+      // T = (I + A)^-1 of the chunk, made by gdr_tinv_kernel, into T buffer c & 1
+      tc::bulk_g2s(sm + OFF_T + (uint32_t)(c & 1) * 8192, tin + (head * nchunks + c) * (kC * 64),
+                   8192, bar);
     };
     auto pmma_wait = [&]() -> bool {
       const bool bad = gwait(bar_pmma, pmma_phase);
       pmma_phase ^= 1u;
       return bad;
     };
-    if (p == 0 && nchunks > 0) issue_raw(0);
+    if (p == 0 && nchunks > 0) issue_load(0);
+    issued = 0;
     float nb_gate = 0.f, ng_gate = 1.f;
     if (p < 64 && p < L) {
       nb_gate = to_f<G>(bh[p]);
@@ -286,7 +298,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
     for (int64_t c = 0; c < nchunks; ++c) {
       const int b = (int)(c & 1);
       const int64_t tok0 = c * kC;
-      const int nvalid = (int)((L - tok0) < kC ? (L - tok0) : kC);
+      const uint32_t QKs = set_base(c), Vs = QKs + 32768;
       uint8_t* G0 = gtab(b);
       float* sLc = reinterpret_cast<float*>(G0 + G_LC);
       int* sZ = reinterpret_cast<int*>(G0 + G_Z);
@@ -295,6 +307,10 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       const GateTabs gt{sLc, sZ, sNeg};
       // buffers QK[b], U[b] and gate table b were last used by chunk c - 2
       if (c >= 2 && gwait(bar_done + b, (uint32_t)(((c - 2) >> 1) & 1))) break;
+      // tile set (c + 1) & 1 and T buffer (c + 1) & 1 were last read by chunk
+      // c - 1, whose MMAs and scaled copies are complete
+      if (p == 0 && c + 1 < nchunks) issue_load(c + 1);
+      if (c + 1 < nchunks) issued = c + 1;
       if (p < 64) {
         const float bt = nb_gate, gg = ng_gate;
         const int64_t t1 = tok0 + kC + p;
@@ -319,42 +335,31 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         sZ[p] = zi;
         sNeg[p] = ng;
       }
-      const bool raw_bad = gwait(bar_raw, raw_phase);
-      raw_phase ^= 1u;
-      if (raw_bad) break;
+      const bool ld_bad = gwait(ld_bar(c), (uint32_t)((c >> 1) & 1));
+      if (ld_bad) break;
+      landed = c;
       if (p >= 32 && p < 64) {
         sLc[p] += sLc[31];
         sZ[p] = max(sZ[p], sZ[31]);
         sNeg[p] += sNeg[31];
       }
-      // RAW (row-major input dtype) -> fp16 swizzled tiles; rows past the end are
-      // zero.  24 chunks of 16 bytes per thread, 8 loads in flight at a time.
+      if constexpr (!std::is_same<T, __half>::value) {
+        // bf16 -> fp16 in place over the set's 48 KB (the swizzle does not
+        // matter elementwise): 24 chunks of 16 bytes per thread, 8 in flight
 #pragma unroll
-      for (int base = p; base < 3 * 1024; base += 8 * 128) {
-        uint4 val[8];
+        for (int u0 = 0; u0 < 24; u0 += 8) {
+          uint4 val[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int idx = base + u * 128;
-          const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
-          val[u] = (t < nvalid) ? *reinterpret_cast<const uint4*>(sm + OFF_RAW + m * 16384 +
-                                                                  t * 256 + ch * 16)
-                                : make_uint4(0, 0, 0, 0);
-        }
+          for (int u = 0; u < 8; ++u)
+            val[u] = *reinterpret_cast<const uint4*>(sm + QKs + (uint32_t)(p + 128 * (u0 + u)) * 16);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int idx = base + u * 128;
-          const int m = idx >> 10, rem = idx & 1023, t = rem >> 4, ch = rem & 15;
-          const int half = ch >> 3, cc = ch & 7;
-          uint32_t off;
-          if (m == 0) off = OFF_QK + half * 16384 + tc::sw128_chunk(t, cc);
-          else if (m == 1) off = OFF_QK + half * 16384 + tc::sw128_chunk(64 + t, cc);
-          else off = OFF_V + half * 8192 + tc::sw128_chunk(t, cc);
-          *reinterpret_cast<uint4*>(sm + off) = to_op8<T>(val[u]);
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(sm + QKs + (uint32_t)(p + 128 * (u0 + u)) * 16) =
+                to_op8<T>(val[u]);
         }
       }
       tc::fence_proxy_async();
       gsync();
-      if (p == 0 && c + 1 < nchunks) issue_raw(c + 1);
       if (p < 64) {
         float* sGam = reinterpret_cast<float*>(G0 + G_GAM);
         float* sGamP = reinterpret_cast<float*>(G0 + G_GAMP);
@@ -372,170 +377,48 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t h = ks >> 2, kk = ks & 3;
-          const uint64_t da = tc::desc_sw128(sb + OFF_QK + h * 16384 + kk * 32, 16, 1024);
-          const uint64_t db = tc::desc_sw128(sb + OFF_QK + h * 16384 + 8192 + kk * 32, 16, 1024);
+          const uint64_t da = tc::desc_sw128(sb + QKs + h * 16384 + kk * 32, 16, 1024);
+          const uint64_t db = tc::desc_sw128(sb + QKs + h * 16384 + 8192 + kk * 32, 16, 1024);
           tc::mma_f16(tm + TM_QK0 + 64 * b, da, db, id_a, ks > 0);
         }
         tc::mma_commit(bar_pmma);
       }
       if (pmma_wait()) break;
-      // ---- A (rows 64-127 of QK[b]): A[t][s] = ratio(t-1,s) beta_s (k_t . k_s), s < t
-      if (quad >= 2) {
-        const int t = row - 64, tr = t - 1;
-        const float lt = tr >= 0 ? sLc[tr] : 0.f;
-        const int zr = tr >= 0 ? sZ[tr] : -1;
-        const float sg = (tr >= 0 && (sNeg[tr] & 1)) ? -1.f : 1.f;
-        const float* sSB = reinterpret_cast<const float*>(G0 + G_SB);
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t r[32];
-          tc::tmem_ld32(tm_lane + TM_QK0 + 64 * b + 32 * hf, r);
-          tc::tmem_wait_ld();
-          float pv[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int s = 32 * hf + j;
-            const bool on = (s <= tr) && (zr <= s);
-            pv[j] = on ? -sg * sSB[s] * ex2(lt - sLc[s]) * __uint_as_float(r[j]) : 0.f;
-          }
-          // stored transposed: sA[s][t] holds -A[t][s], so column s is contiguous
-#pragma unroll
-          for (int j = 0; j < 32; ++j) sA[(32 * hf + j) * kAStride + t] = pv[j];
-        }
-      }
-      // gQ, Kt and T overwrite chain inputs of chunk c - 1: wait for its last MMAs
+      // gQ, Kt and gK overwrite chain inputs of chunk c - 1: wait for its last MMAs
       if (c >= 1) {
         if (gwait(bar_b2, (uint32_t)((c - 1) & 1))) break;
       } else {
         gsync();
       }
-      // ---- T = (I + A)^-1 by 32x32 blocks.  With N = -A (sA holds N
-      // transposed: sA[c][r] = N[r][c], zero on and above the diagonal),
-      // T = (I - N)^-1 has diagonal blocks T_II = (I - N_II)^-1 and
-      // T10 = T11 N10 T00.  The diagonal blocks are solved column by column
-      // (right-looking: once t_i is final its contribution goes to every later
-      // row, a 31-FMA dependency chain) by 64 threads while the other 64 make
-      // the scaled copies; then all 128 form P = N10 T00 and T10 = T11 P.
-      // Scratch: fp32 T00 | T11 in the P tile (free until the chain's next (f)),
-      // P in the unused upper triangle of sA.
-      float* Tsc = reinterpret_cast<float*>(sm + OFF_P);  // [2][32][32]
-      if (p < 64) {
-        const int I = p >> 5, cc = p & 31;
-        const float* nb = sA + (32 * I) * kAStride + 32 * I;  // nb[i][a] = N[32I+a][32I+i]
-        float2 col[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r)
-          col[r] = make_float2((2 * r == cc) ? 1.f : 0.f, (2 * r + 1 == cc) ? 1.f : 0.f);
-#pragma unroll
-        for (int i = 0; i < 31; ++i) {
-          const float ti = (i & 1) ? col[i / 2].y : col[i / 2].x;
-          const float2 t2 = make_float2(ti, ti);
-          const float* nc = nb + i * kAStride;
-          int r = i + 1;
-          if (r & 1) {  // row i + 1 shares its pair with the final row i
-            col[r / 2].y = fmaf(nc[r], ti, col[r / 2].y);
-            ++r;
-          }
-          if ((r & 3) && r < 32) {  // one pair up to a 4-row boundary
-            const float2 a2 = *reinterpret_cast<const float2*>(nc + r);
-            col[r / 2] = fma2(a2, t2, col[r / 2]);
-            r += 2;
-          }
-#pragma unroll
-          for (; r < 32; r += 4) {
-            const float4 a4 = *reinterpret_cast<const float4*>(nc + r);
-            col[r / 2] = fma2(make_float2(a4.x, a4.y), t2, col[r / 2]);
-            col[r / 2 + 1] = fma2(make_float2(a4.z, a4.w), t2, col[r / 2 + 1]);
-          }
-        }
-        // fp32 copy for T10; fp16 T tile [t][s]: rows of block I in column p,
-        // and zeros above the diagonal (rows 0-31 of columns 32-63)
-#pragma unroll
-        for (int a = 0; a < 32; ++a) {
-          const float tv = (a & 1) ? col[a / 2].y : col[a / 2].x;
-          Tsc[(32 * I + a) * 32 + cc] = tv;
-          *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(32 * I + a, p)) =
-              __float2half_rn(tv);
-          if (I == 1)
-            *reinterpret_cast<__half*>(sm + OFF_WT + tc::sw128_off(a, p)) = __float2half_rn(0.f);
-        }
-      } else {
+      {
         // ---- scaled copies: gQ -> GQ, Kt -> KT, gK in place; 8 loads in flight
         const float* sGam = reinterpret_cast<const float*>(G0 + G_GAM);
         const float* sGamP = reinterpret_cast<const float*>(G0 + G_GAMP);
         const float* sKts = reinterpret_cast<const float*>(G0 + G_KTS);
-        const int pc = p - 64;
 #pragma unroll
         for (int m = 0; m < 2; ++m) {  // m = 0: Q rows (0-63), m = 1: K rows (64-127)
+          uint4 raw[8];
 #pragma unroll
-          for (int bt = 0; bt < 2; ++bt) {
-            uint4 raw[8];
+          for (int u = 0; u < 8; ++u) {
+            const int rem = p + 128 * u, t = rem >> 4, ch = rem & 15;
+            raw[u] = *reinterpret_cast<const uint4*>(sm + QKs + (ch >> 3) * 16384 +
+                                                     tc::sw128_chunk(64 * m + t, ch & 7));
+          }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int rem = pc + 64 * (8 * bt + u), t = rem >> 4, ch = rem & 15;
-              raw[u] = *reinterpret_cast<const uint4*>(sm + OFF_QK + (ch >> 3) * 16384 +
-                                                       tc::sw128_chunk(64 * m + t, ch & 7));
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int rem = pc + 64 * (8 * bt + u), t = rem >> 4, ch = rem & 15;
-              const int half = ch >> 3, cc = ch & 7;
-              if (m == 0) {
-                *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
-                    scale8h(raw[u], __float2half2_rn(sGam[t]));
-              } else {
-                *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
-                    scale8h(raw[u], __float2half2_rn(sKts[t]));
-                *reinterpret_cast<uint4*>(sm + OFF_QK + half * 16384 +
-                                          tc::sw128_chunk(64 + t, cc)) =
-                    scale8h(raw[u], __float2half2_rn(sGamP[t]));
-              }
+          for (int u = 0; u < 8; ++u) {
+            const int rem = p + 128 * u, t = rem >> 4, ch = rem & 15;
+            const int half = ch >> 3, cc = ch & 7;
+            if (m == 0) {
+              *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
+                  scale8h(raw[u], __float2half2_rn(sGam[t]));
+            } else {
+              *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
+                  scale8h(raw[u], __float2half2_rn(sKts[t]));
+              *reinterpret_cast<uint4*>(sm + QKs + half * 16384 + tc::sw128_chunk(64 + t, cc)) =
+                  scale8h(raw[u], __float2half2_rn(sGamP[t]));
             }
           }
         }
-      }
-      gsync();
-      {
-        // ---- P = N10 T00 -> sA[32 + a][b] (the slots of N[b][32 + a], above the diagonal)
-        const int a = p >> 2, b0 = (p & 3) * 8;
-        float2 acc[4] = {};
-#pragma unroll
-        for (int d = 0; d < 32; ++d) {
-          const float n = sA[d * kAStride + 32 + a];  // N[32 + a][d]
-          const float2 n2 = make_float2(n, n);
-          const float4 t0 = *reinterpret_cast<const float4*>(Tsc + d * 32 + b0);
-          const float4 t1 = *reinterpret_cast<const float4*>(Tsc + d * 32 + b0 + 4);
-          acc[0] = fma2(n2, make_float2(t0.x, t0.y), acc[0]);
-          acc[1] = fma2(n2, make_float2(t0.z, t0.w), acc[1]);
-          acc[2] = fma2(n2, make_float2(t1.x, t1.y), acc[2]);
-          acc[3] = fma2(n2, make_float2(t1.z, t1.w), acc[3]);
-        }
-        float* prow = sA + (32 + a) * kAStride + b0;
-        *reinterpret_cast<float4*>(prow) = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
-        *reinterpret_cast<float4*>(prow + 4) = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
-      }
-      gsync();
-      {
-        // ---- T10 = T11 P -> rows 32-63, columns 0-31 of the T tile
-        const int a = p >> 2, b0 = (p & 3) * 8;
-        float2 acc[4] = {};
-#pragma unroll
-        for (int c2 = 0; c2 < 32; ++c2) {
-          const float tv = Tsc[(32 + a) * 32 + c2];  // T11[a][c2]
-          const float2 t2 = make_float2(tv, tv);
-          const float4 p0 = *reinterpret_cast<const float4*>(sA + (32 + c2) * kAStride + b0);
-          const float4 p1 = *reinterpret_cast<const float4*>(sA + (32 + c2) * kAStride + b0 + 4);
-          acc[0] = fma2(t2, make_float2(p0.x, p0.y), acc[0]);
-          acc[1] = fma2(t2, make_float2(p0.z, p0.w), acc[1]);
-          acc[2] = fma2(t2, make_float2(p1.x, p1.y), acc[2]);
-          acc[3] = fma2(t2, make_float2(p1.z, p1.w), acc[3]);
-        }
-        uint4 pk;
-        pk.x = pack2<Op>(acc[0].x, acc[0].y);
-        pk.y = pack2<Op>(acc[1].x, acc[1].y);
-        pk.z = pack2<Op>(acc[2].x, acc[2].y);
-        pk.w = pack2<Op>(acc[3].x, acc[3].y);
-        *reinterpret_cast<uint4*>(sm + OFF_WT + tc::sw128_chunk(32 + a, b0 >> 3)) = pk;
       }
       tc::fence_proxy_async();
       gsync();
@@ -544,9 +427,9 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         constexpr uint32_t id_mn = tc::idesc_f16(128, 64, BF, true, false);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t dt = tc::desc_sw128(sb + OFF_WT + ks * 32, 16, 1024);
-          const uint64_t dk = tc::desc_sw128(sb + OFF_QK + 8192 + ks * 2048, 16384, 1024);
-          const uint64_t dv = tc::desc_sw128(sb + OFF_V + ks * 2048, 8192, 1024);
+          const uint64_t dt = tc::desc_sw128(sb + OFF_T + (uint32_t)b * 8192 + ks * 32, 16, 1024);
+          const uint64_t dk = tc::desc_sw128(sb + QKs + 8192 + ks * 2048, 16384, 1024);
+          const uint64_t dv = tc::desc_sw128(sb + Vs + ks * 2048, 8192, 1024);
           tc::mma_f16(tm + TM_W, dk, dt, id_mn, ks > 0);
           tc::mma_f16(tm + TM_U0 + 64 * b, dv, dt, id_mn, ks > 0);
         }
@@ -574,8 +457,10 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       if (p == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar_prep))
                                : "memory");
     }
-    // an abort can leave one bulk copy in flight: let it land before exiting
-    if (*s_abort && p == 0) tc::mbar_wait(bar_raw, raw_phase, kWaitLimit);
+    // an abort can leave tile loads in flight: let them land before exiting
+    if (*s_abort && p == 0)
+      for (int64_t c = landed + 1; c <= issued; ++c)
+        tc::mbar_wait(ld_bar(c), (uint32_t)((c >> 1) & 1), kWaitLimit);
   } else {
     // =====================================================================
     // chain warps: the state-dependent part of each chunk
@@ -798,10 +683,303 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   }
 }
 
+// ---------------------------------------------------------------------------
+// T = (I + A)^-1 of every (head, chunk): the one step of a chunk's preparation
+// with a long dependency chain (the triangular solve), run for all chunks in
+// parallel before the scan kernel, with several CTAs per SM hiding each
+// other's latency.  Output: per (head, chunk) the fp16 T tile [t][s] in the
+// 128-byte-swizzled layout the scan kernel's MMAs read (8 KB), copied there
+// as it is.
+// ---------------------------------------------------------------------------
+constexpr int kTiThr = 128;
+constexpr uint32_t TI_K = 0;         // fp16 2 x [128 x 128B]: rows 0-63 K, rows 64-127 K again,
+                                     // so K K^T lands in all four TMEM lane quadrants
+constexpr uint32_t TI_OUT = 32768;   // fp16 T tile [64 x 128B]
+constexpr uint32_t TI_A = 40960;     // fp32 [64][68]: N = -A stored transposed
+constexpr uint32_t TI_TSC = 58368;   // fp32 [2][32][32]: T00 | T11
+constexpr uint32_t TI_G = 66560;     // lc, z, neg, signed beta: 64 each
+constexpr uint32_t TI_BAR = 67584;   // mbarrier, TMEM address
+constexpr uint32_t kTiSmem = TI_BAR + 64 + 1024;  // + alignment slack
+constexpr uint32_t kTiCols = 64;
+
+template <typename T, typename G>
+__global__ void __launch_bounds__(kTiThr, 3)
+gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __restrict__ g,
+                __half* __restrict__ tout, int64_t L, int64_t items) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~(uintptr_t)1023);
+  const uint32_t sb = tc::smem_u32(sm);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + TI_BAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + TI_BAR + 16);
+  float* sA = reinterpret_cast<float*>(sm + TI_A);
+  float* Tsc = reinterpret_cast<float*>(sm + TI_TSC);
+  float* sLc = reinterpret_cast<float*>(sm + TI_G);
+  int* sZ = reinterpret_cast<int*>(sm + TI_G + 256);
+  int* sNeg = reinterpret_cast<int*>(sm + TI_G + 512);
+  float* sSB = reinterpret_cast<float*>(sm + TI_G + 768);
+  const int p = threadIdx.x, lane = p & 31, warp = p >> 5;
+  const int64_t nchunks = (L + kC - 1) / kC;
+  if (warp == 0) {
+    tc::tmem_alloc(s_tmem, kTiCols);
+    tc::tmem_relinquish();
+  }
+  if (p == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tm = *s_tmem;
+  const uint32_t tm_lane = tm + ((uint32_t)(32 * (warp & 3)) << 16);
+  uint32_t phase = 0;
+
+  // the k rows of an item: chunk j = p + 128 u of the 1024 16-byte chunks
+  uint4 val[8];
+  float bt = 0.f, gg = 1.f;
+  auto fetch = [&](int64_t it) {
+    if (it >= items) return;
+    const int64_t head = it / nchunks, c = it % nchunks;
+    const int64_t t0 = c * kC;
+    const int nvalid = (int)((L - t0) < kC ? (L - t0) : kC);
+    const T* kr = k + (head * L + t0) * kD;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = p + 128 * u, t = idx >> 4, ch = idx & 15;
+      val[u] = t < nvalid ? ld_global_stream_v4(kr + t * kD + ch * 8) : make_uint4(0, 0, 0, 0);
+    }
+    if (p < 64) {
+      bt = p < nvalid ? to_f<G>(beta[head * L + t0 + p]) : 0.f;
+      gg = p < nvalid ? to_f<G>(g[head * L + t0 + p]) : 1.f;
+    }
+  };
+  fetch(blockIdx.x);
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    // ---- fp16 K tile and gate tables
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = p + 128 * u, t = idx >> 4, ch = idx & 15;
+      const uint4 h = to_op8<T>(val[u]);
+      *reinterpret_cast<uint4*>(sm + TI_K + (ch >> 3) * 16384 + tc::sw128_chunk(t, ch & 7)) = h;
+      *reinterpret_cast<uint4*>(sm + TI_K + (ch >> 3) * 16384 + tc::sw128_chunk(64 + t, ch & 7)) =
+          h;
+    }
+    if (p < 64) {
+      float lg = (gg != 0.f) ? log2f(fabsf(gg)) : 0.f;
+      int zi = (gg == 0.f) ? p : -1;
+      int ng = (gg < 0.f) ? 1 : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float a = __shfl_up_sync(0xffffffffu, lg, off);
+        const int bz = __shfl_up_sync(0xffffffffu, zi, off);
+        const int bn = __shfl_up_sync(0xffffffffu, ng, off);
+        if (lane >= off) {
+          lg += a;
+          zi = max(zi, bz);
+          ng += bn;
+        }
+      }
+      sLc[p] = lg;
+      sZ[p] = zi;
+      sNeg[p] = ng;
+      sSB[p] = bt;
+    }
+    fetch(it + gridDim.x);  // the next item's loads fly during this one
+    tc::fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (p >= 32 && p < 64) {
+      sLc[p] += sLc[31];
+      sZ[p] = max(sZ[p], sZ[31]);
+      sNeg[p] += sNeg[31];
+    }
+    // ---- K K^T (TMEM lanes 0-63)
+    if (p == 0) {
+      constexpr uint32_t id = tc::idesc_f16(128, 64, false, false, false);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t h = ks >> 2, kk = ks & 3;
+        const uint64_t d = tc::desc_sw128(sb + TI_K + h * 16384 + kk * 32, 16, 1024);
+        tc::mma_f16(tm, d, d, id, ks > 0);  // A: all 128 rows; B: rows 0-63
+      }
+      tc::mma_commit(bar);
+    }
+    __syncthreads();
+    if (p < 64) sSB[p] = (sNeg[p] & 1) ? -sSB[p] : sSB[p];
+    int good = 1;
+    if (p == 0) good = tc::mbar_wait(bar, phase, kWaitLimit) ? 1 : 0;  // one poller
+    phase ^= 1u;
+    if (!__syncthreads_and(good)) {
+      if (p == 0) atomicAdd(&g_gdr_timeouts, 1u);
+      break;
+    }
+    tc::fence_after_sync();
+    // ---- N = -A, stored transposed: sA[s][t] = -ratio(t-1,s) beta_s (k_t . k_s), s < t
+    {
+      // warps 0, 1: rows 0-63 (lanes 0-63), columns 0-31; warps 2, 3: the same
+      // rows from the copy in lanes 64-127, columns 32-63
+      const int t = 32 * (warp & 1) + lane, tr = t - 1, hf = warp >> 1;
+      const float lt = tr >= 0 ? sLc[tr] : 0.f;
+      const int zr = tr >= 0 ? sZ[tr] : -1;
+      const float sg = (tr >= 0 && (sNeg[tr] & 1)) ? -1.f : 1.f;
+      {
+        uint32_t r[32];
+        tc::tmem_ld32(tm_lane + 32 * hf, r);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int s = 32 * hf + j;
+          const bool on = (s <= tr) && (zr <= s);
+          sA[s * kAStride + t] = on ? -sg * sSB[s] * ex2(lt - sLc[s]) * __uint_as_float(r[j]) : 0.f;
+        }
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    // ---- diagonal 32x32 blocks of T = (I - N)^-1, column by column (right-looking)
+    if (p < 64) {
+      const int I = p >> 5, cc = p & 31;
+      const float* nb = sA + (32 * I) * kAStride + 32 * I;  // nb[i][a] = N[32I+a][32I+i]
+      float2 col[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r)
+        col[r] = make_float2((2 * r == cc) ? 1.f : 0.f, (2 * r + 1 == cc) ? 1.f : 0.f);
+#pragma unroll
+      for (int i = 0; i < 31; ++i) {
+        const float ti = (i & 1) ? col[i / 2].y : col[i / 2].x;
+        const float2 t2 = make_float2(ti, ti);
+        const float* nc = nb + i * kAStride;
+        int r = i + 1;
+        if (r & 1) {
+          col[r / 2].y = fmaf(nc[r], ti, col[r / 2].y);
+          ++r;
+        }
+        if ((r & 3) && r < 32) {
+          const float2 a2 = *reinterpret_cast<const float2*>(nc + r);
+          col[r / 2] = fma2(a2, t2, col[r / 2]);
+          r += 2;
+        }
+#pragma unroll
+        for (; r < 32; r += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(nc + r);
+          col[r / 2] = fma2(make_float2(a4.x, a4.y), t2, col[r / 2]);
+          col[r / 2 + 1] = fma2(make_float2(a4.z, a4.w), t2, col[r / 2 + 1]);
+        }
+      }
+#pragma unroll
+      for (int a = 0; a < 32; ++a) {
+        const float tv = (a & 1) ? col[a / 2].y : col[a / 2].x;
+        Tsc[(32 * I + a) * 32 + cc] = tv;
+        *reinterpret_cast<__half*>(sm + TI_OUT + tc::sw128_off(32 * I + a, p)) = __float2half_rn(tv);
+        if (I == 1)
+          *reinterpret_cast<__half*>(sm + TI_OUT + tc::sw128_off(a, p)) = __float2half_rn(0.f);
+      }
+    }
+    __syncthreads();
+    {
+      // ---- P = N10 T00 -> sA[32 + a][b] (slots above the diagonal)
+      const int a = p >> 2, b0 = (p & 3) * 8;
+      float2 acc[4] = {};
+#pragma unroll
+      for (int d = 0; d < 32; ++d) {
+        const float n = sA[d * kAStride + 32 + a];
+        const float2 n2 = make_float2(n, n);
+        const float4 t0 = *reinterpret_cast<const float4*>(Tsc + d * 32 + b0);
+        const float4 t1 = *reinterpret_cast<const float4*>(Tsc + d * 32 + b0 + 4);
+        acc[0] = fma2(n2, make_float2(t0.x, t0.y), acc[0]);
+        acc[1] = fma2(n2, make_float2(t0.z, t0.w), acc[1]);
+        acc[2] = fma2(n2, make_float2(t1.x, t1.y), acc[2]);
+        acc[3] = fma2(n2, make_float2(t1.z, t1.w), acc[3]);
+      }
+      float* prow = sA + (32 + a) * kAStride + b0;
+      *reinterpret_cast<float4*>(prow) = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
+      *reinterpret_cast<float4*>(prow + 4) = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
+    }
+    __syncthreads();
+    {
+      // ---- T10 = T11 P -> rows 32-63, columns 0-31 of the T tile
+      const int a = p >> 2, b0 = (p & 3) * 8;
+      float2 acc[4] = {};
+#pragma unroll
+      for (int c2 = 0; c2 < 32; ++c2) {
+        const float tv = Tsc[(32 + a) * 32 + c2];
+        const float2 t2 = make_float2(tv, tv);
+        const float4 p0 = *reinterpret_cast<const float4*>(sA + (32 + c2) * kAStride + b0);
+        const float4 p1 = *reinterpret_cast<const float4*>(sA + (32 + c2) * kAStride + b0 + 4);
+        acc[0] = fma2(t2, make_float2(p0.x, p0.y), acc[0]);
+        acc[1] = fma2(t2, make_float2(p0.z, p0.w), acc[1]);
+        acc[2] = fma2(t2, make_float2(p1.x, p1.y), acc[2]);
+        acc[3] = fma2(t2, make_float2(p1.z, p1.w), acc[3]);
+      }
+      uint4 pk;
+      pk.x = pack2<Op>(acc[0].x, acc[0].y);
+      pk.y = pack2<Op>(acc[1].x, acc[1].y);
+      pk.z = pack2<Op>(acc[2].x, acc[2].y);
+      pk.w = pack2<Op>(acc[3].x, acc[3].y);
+      *reinterpret_cast<uint4*>(sm + TI_OUT + tc::sw128_chunk(32 + a, b0 >> 3)) = pk;
+    }
+    __syncthreads();
+    // ---- the 8 KB tile to global memory as it is
+    {
+      uint4* dst = reinterpret_cast<uint4*>(tout + it * (int64_t)(kC * 64));
+      const uint4* srcv = reinterpret_cast<const uint4*>(sm + TI_OUT);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dst[p + 128 * u] = srcv[p + 128 * u];
+    }
+    __syncthreads();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tm, kTiCols);
+  }
+}
+
 template <typename T, typename G>
 int launch_tc(const void* q, const void* k, const void* v, const void* beta, const void* g,
-              const float* h0, void* o, float* hT, int* flags, int64_t BH, int64_t L,
-              cudaStream_t st) {
+              const float* h0, void* o, float* hT, int* flags, __half* tbuf, int64_t BH,
+              int64_t L, cudaStream_t st) {
+  // 1. T = (I + A)^-1 of every (head, chunk), all chunks in parallel
+  auto tkern = gdr_tinv_kernel<T, G>;
+  // several CTAs per SM hide each other's latency: ask for the largest shared
+  // memory carve-out so that they fit
+  if (cudaFuncSetAttribute(tkern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTiSmem) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(tkern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
+    set_error("gdr_tinv_kernel: cannot reserve %u bytes of shared memory", kTiSmem);
+    return FO_ECUDA;
+  }
+  // 3 CTAs per SM (shared memory and registers allow it); the CTAs never wait
+  // on one another, so more of them than fit simply queue
+  const int64_t items = BH * ((L + kC - 1) / kC);
+  int64_t tgrid = (int64_t)num_sms() * 3;
+  if (tgrid > items) tgrid = items;
+  tkern<<<(unsigned)tgrid, kTiThr, kTiSmem, st>>>((const T*)k, (const G*)beta, (const G*)g, tbuf,
+                                                  L, items);
+  if (int rc = check_launch("gdr_tinv_kernel")) return rc;
+  // 2. the chunk scan; q, k, v reach it through TMA tensor maps
+  CUtensorMap maps[3];
+  const void* srcs[3] = {q, k, v};
+  const cuuint64_t gdim[3] = {(cuuint64_t)kD, (cuuint64_t)L, (cuuint64_t)BH};
+  const cuuint64_t gstride[2] = {(cuuint64_t)kD * sizeof(T), (cuuint64_t)L * kD * sizeof(T)};
+  const cuuint32_t box[3] = {64, (cuuint32_t)kC, 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  for (int i = 0; i < 3; ++i) {
+    const CUresult r = cuTensorMapEncodeTiled(
+        &maps[i], std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+        3, const_cast<void*>(srcs[i]), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("chunk_gated_delta_rule: cuTensorMapEncodeTiled failed (%d)", (int)r);
+      return FO_ECUDA;
+    }
+  }
   auto kern = gdr_tc_kernel<T, G>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
       cudaSuccess) {
@@ -810,19 +988,19 @@ int launch_tc(const void* q, const void* k, const void* v, const void* beta, con
   }
   kern<<<(unsigned)BH, kThr, kSmemBytes, st>>>((const T*)q, (const T*)k, (const T*)v,
                                                (const G*)beta, (const G*)g, h0, (T*)o, hT, flags,
-                                               L);
+                                               tbuf, maps[0], maps[1], maps[2], L);
   return check_launch("gdr_tc_kernel");
 }
 
 template <typename T>
 int tc_gate_dispatch(int gate_dtype, const void* q, const void* k, const void* v, const void* beta,
-                     const void* g, const float* h0, void* o, float* hT, int* flags, int64_t BH,
-                     int64_t L, cudaStream_t st) {
+                     const void* g, const float* h0, void* o, float* hT, int* flags,
+                     __half* tbuf, int64_t BH, int64_t L, cudaStream_t st) {
   switch (gate_dtype) {
-    case FO_F32: return launch_tc<T, float>(q, k, v, beta, g, h0, o, hT, flags, BH, L, st);
-    case FO_F16: return launch_tc<T, __half>(q, k, v, beta, g, h0, o, hT, flags, BH, L, st);
+    case FO_F32: return launch_tc<T, float>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, st);
+    case FO_F16: return launch_tc<T, __half>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, st);
     case FO_BF16:
-      return launch_tc<T, __nv_bfloat16>(q, k, v, beta, g, h0, o, hT, flags, BH, L, st);
+      return launch_tc<T, __nv_bfloat16>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, st);
   }
   set_error("chunk_gated_delta_rule: unsupported gate dtype code %d", gate_dtype);
   return FO_EDTYPE;
@@ -916,6 +1094,8 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const __nv_bfloat16* _
 using namespace fo;
 
 namespace {
+inline int64_t gdr_flags_bytes(int64_t heads) { return (heads * (int64_t)sizeof(int) + 255) & ~(int64_t)255; }
+
 inline bool gdr_tc_eligible(const void* q, const void* k, const void* v, const void* o,
                             const float* hT, int64_t D, int dtype) {
   return D == 128 && (dtype == FO_BF16 || dtype == FO_F16) && aligned16(q) && aligned16(k) &&
@@ -927,8 +1107,14 @@ extern "C" int fo_gdr_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t D
                                       int64_t* bytes) {
   clear_error();
   FO_CHECK_ARG(bytes && B >= 0 && H >= 0 && L >= 0, "fo_gdr_workspace_bytes: bad argument");
-  // the tensor-core path keeps one int flag per head (fp16 range guard)
-  *bytes = (D == 128 && (dtype == FO_BF16 || dtype == FO_F16)) ? B * H * (int64_t)sizeof(int) : 0;
+  // the tensor-core path: one int flag per head (fp16 range guard), then the
+  // fp16 T tile of every (head, chunk) (8 KB each, 256-byte aligned)
+  if (D == 128 && (dtype == FO_BF16 || dtype == FO_F16)) {
+    const int64_t nc = (L + kC - 1) / kC;
+    *bytes = gdr_flags_bytes(B * H) + B * H * nc * 8192;
+  } else {
+    *bytes = 0;
+  }
   return FO_OK;
 }
 
@@ -955,17 +1141,20 @@ extern "C" int fo_gdr_fwd(const void* q, const void* k, const void* v, const voi
     return FO_OK;
   }
   if (gdr_tc_eligible(q, k, v, o, hT, D, dtype)) {
-    const int64_t need = B * H * (int64_t)sizeof(int);
-    if (!workspace || ws_bytes < need) {
-      set_error("chunk_gated_delta_rule: workspace of %lld bytes required, got %lld",
+    int64_t need = 0;
+    fo_gdr_workspace_bytes(B, H, L, D, dtype, &need);
+    if (!workspace || ws_bytes < need || !aligned16(workspace)) {
+      set_error("chunk_gated_delta_rule: 16-byte-aligned workspace of %lld bytes required, got %lld",
                 (long long)need, (long long)ws_bytes);
       return FO_EWORKSPACE;
     }
     int* flags = reinterpret_cast<int*>(workspace);
+    __half* tbuf = reinterpret_cast<__half*>(reinterpret_cast<char*>(workspace) +
+                                             gdr_flags_bytes(B * H));
     int rc = dtype == FO_BF16 ? tc_gate_dispatch<__nv_bfloat16>(gate_dtype, q, k, v, beta, g, h0,
-                                                                o, hT, flags, B * H, L, st)
+                                                                o, hT, flags, tbuf, B * H, L, st)
                               : tc_gate_dispatch<__half>(gate_dtype, q, k, v, beta, g, h0, o, hT,
-                                                         flags, B * H, L, st);
+                                                         flags, tbuf, B * H, L, st);
     if (rc) return rc;
     // heads whose fp16 operands left the fp16 range: exact fp32 per-step recomputation
     // (every other head's CTA returns at once)
