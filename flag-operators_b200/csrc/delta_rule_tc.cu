@@ -785,7 +785,6 @@ gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __
       sNeg[p] = ng;
       sSB[p] = bt;
     }
-    fetch(it + gridDim.x);  // the next item's loads fly during this one
     tc::fence_proxy_async();
     tc::fence_before_sync();
     __syncthreads();
@@ -806,6 +805,7 @@ gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __
       }
       tc::mma_commit(bar);
     }
+    fetch(it + gridDim.x);  // the next item's loads fly during this one
     __syncthreads();
     if (p < 64) sSB[p] = (sNeg[p] & 1) ? -sSB[p] : sSB[p];
     int good = 1;
