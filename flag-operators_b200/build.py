@@ -67,7 +67,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         objs = list(ex.map(lambda s: _compile(s, force, verbose), srcs))
     if (force or not os.path.exists(LIB)
             or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs)):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

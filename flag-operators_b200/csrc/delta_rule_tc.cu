@@ -35,6 +35,7 @@
 // the operand of (d)/(e)).  The 64x64 triangular inverse is a blocked forward
 // substitution in fp32 on the CUDA cores.  One CTA per (batch, head).
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <math.h>
 
 #include "common.cuh"
@@ -938,6 +939,22 @@ gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __
   }
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so that the
+// library has no link-time dependency on the driver library (it loads on
+// machines without a GPU driver; the entry point is looked up on first use).
+PFN_cuTensorMapEncodeTiled tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
+  }
+  return fn;
+}
+
 template <typename T, typename G>
 int launch_tc(const void* q, const void* k, const void* v, const void* beta, const void* g,
               const float* h0, void* o, float* hT, int* flags, __half* tbuf, int64_t BH,
@@ -968,8 +985,13 @@ int launch_tc(const void* q, const void* k, const void* v, const void* beta, con
   const cuuint64_t gstride[2] = {(cuuint64_t)kD * sizeof(T), (cuuint64_t)L * kD * sizeof(T)};
   const cuuint32_t box[3] = {64, (cuuint32_t)kC, 1};
   const cuuint32_t estride[3] = {1, 1, 1};
+  PFN_cuTensorMapEncodeTiled encode = tensor_map_encoder();
+  if (!encode) {
+    set_error("chunk_gated_delta_rule: the driver's cuTensorMapEncodeTiled is not available");
+    return FO_ECUDA;
+  }
   for (int i = 0; i < 3; ++i) {
-    const CUresult r = cuTensorMapEncodeTiled(
+    const CUresult r = encode(
         &maps[i], std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
         3, const_cast<void*>(srcs[i]), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
