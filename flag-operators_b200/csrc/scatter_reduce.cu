@@ -491,6 +491,257 @@ __global__ void scatter_finalize_kernel(T* __restrict__ out,
 }
 
 // ---------------------------------------------------------------------------
+// destination-binned path (1-D contiguous updates, 4-byte accumulators, many
+// updates): instead of one L2 atomic per update, three passes
+//   count: updates per output slice of kSliceCells cells (shared histogram),
+//   bin:   (slice << 13 | cell, value) pairs written slice-contiguously (each
+//          CTA sorts a batch of 4096 updates by slice in shared memory and
+//          appends every slice's run at a cursor reserved with one atomic),
+//   reduce: segments of <= kSeg pairs of one slice applied to a dense
+//          shared-memory copy of the slice, then merged into the accumulator
+//          with one global operation per touched cell.
+// The accumulator layout, init and finalize are those of the atomic path.
+// Costs ~2.8x the algorithmic bytes, but at HBM rate instead of the L2's
+// atomic request rate, and products need no global compare-and-swap loop per
+// update.
+// ---------------------------------------------------------------------------
+constexpr int kSliceLog = 13;
+constexpr int kSliceCells = 1 << kSliceLog;
+constexpr int kMaxSlices = 1024;
+constexpr int kBinBatch = 4096;  // updates per CTA step of the bin pass (512 threads x 8)
+constexpr int64_t kSeg = 65536;   // pairs per reduce segment
+constexpr int64_t kBinMinUpdates = (int64_t)1 << 20;
+constexpr size_t kBinHeaderBytes = 12288;  // totals, cursors, work counter
+
+// 4-byte accumulator <-> the 32 bits of a pair entry (bit copies, not value casts)
+template <typename A> __device__ __forceinline__ uint32_t acc_bits(A v) {
+  static_assert(sizeof(A) == 4, "4-byte accumulators");
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  return u;
+}
+template <typename A> __device__ __forceinline__ A acc_from_bits(uint32_t u) {
+  A v;
+  memcpy(&v, &u, 4);
+  return v;
+}
+
+// Exclusive scan of v[0..n) (n <= 1024) into out[0..n] (out[n] = total) by a
+// 512-thread block; v and out may alias.
+__device__ __forceinline__ void block_scan_1024(const uint32_t* v, uint32_t* out, int n,
+                                                uint32_t* warp_tot) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const uint32_t a = (2 * t < n) ? v[2 * t] : 0u, b = (2 * t + 1 < n) ? v[2 * t + 1] : 0u;
+  uint32_t x = a + b;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    uint32_t z = lane < 16 ? warp_tot[lane] : 0u;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, z, o);
+      if (lane >= o) z += y;
+    }
+    if (lane < 16) warp_tot[lane] = z;  // inclusive warp totals
+  }
+  __syncthreads();
+  const uint32_t before = (w > 0 ? warp_tot[w - 1] : 0u) + x - (a + b);
+  if (2 * t < n) out[2 * t] = before;
+  if (2 * t + 1 < n) out[2 * t + 1] = before + a;
+  if (t == 0) out[n] = warp_tot[15];
+  __syncthreads();
+}
+
+template <typename I>
+__global__ void __launch_bounds__(512)
+bin_count_kernel(const I* __restrict__ index, int64_t n, int64_t out_dim, int64_t ostr, int ns,
+                 uint32_t* __restrict__ tot) {
+  __shared__ uint32_t h[kMaxSlices];
+  for (int i = threadIdx.x; i < ns; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+#pragma unroll 4
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += stride) {
+    const int64_t iv = (int64_t)index[p];
+    if (iv >= 0 && iv < out_dim) atomicAdd(&h[(iv * ostr) >> kSliceLog], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < ns; i += blockDim.x)
+    if (h[i]) atomicAdd(&tot[i], h[i]);
+}
+
+template <typename T, typename I, int OP, bool KEYS>
+__global__ void __launch_bounds__(512)
+bin_pairs_kernel(const T* __restrict__ src, const I* __restrict__ index, int64_t n,
+                 int64_t out_dim, int64_t ostr, int ns, const uint32_t* __restrict__ tot,
+                 uint32_t* __restrict__ cursor, uint2* __restrict__ pairs,
+                 int32_t* __restrict__ err) {
+  using AT = Acc<T, OP, KEYS>;
+  using A = typename AT::A;
+  static_assert(sizeof(A) == 4, "4-byte accumulators");
+  __shared__ uint32_t s_start[kMaxSlices + 1];  // first pair of each slice
+  __shared__ uint32_t s_cnt[kMaxSlices + 1];    // this batch: updates per slice, then offsets
+  __shared__ uint32_t s_base[kMaxSlices];       // this batch: the slice run's place in the slice
+  __shared__ uint32_t s_wt[16];
+  __shared__ uint2 s_buf[kBinBatch];
+  const int t = threadIdx.x;
+  block_scan_1024(tot, s_start, ns, s_wt);
+  int32_t bad = 0;
+  // this thread's 8 updates of a batch, loaded one batch ahead
+  int64_t niv[8];
+  T nsv[8];
+  uint32_t nin = 0;  // bit u: update u exists (not past the end)
+  auto load_batch = [&](int64_t b0) {
+    nin = 0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t p = b0 + t + 512 * u;
+      if (p < n) {
+        niv[u] = (int64_t)index[p];
+        nsv[u] = src[p];
+        nin |= 1u << u;
+      }
+    }
+  };
+  const int64_t bstep = (int64_t)gridDim.x * kBinBatch;
+  load_batch((int64_t)blockIdx.x * kBinBatch);
+  for (int64_t b0 = (int64_t)blockIdx.x * kBinBatch; b0 < n; b0 += bstep) {
+    for (int i = t; i < ns; i += 512) s_cnt[i] = 0;
+    int64_t iv_[8];
+    T sv_[8];
+    const uint32_t in_ = nin;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      iv_[u] = niv[u];
+      sv_[u] = nsv[u];
+    }
+    load_batch(b0 + bstep);
+    __syncthreads();
+    uint32_t w0[8], w1[8], lpos[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      w0[u] = 0xffffffffu;
+      if (!((in_ >> u) & 1u)) continue;
+      const int64_t iv = iv_[u];
+      if (iv >= 0 && iv < out_dim) {
+        const int64_t off = iv * ostr;
+        w0[u] = (uint32_t)off;  // (slice << 13) | cell: off < ns * 8192 <= 2^23
+        w1[u] = acc_bits<A>(AT::from(sv_[u]));
+        lpos[u] = atomicAdd(&s_cnt[off >> kSliceLog], 1u);
+      } else {
+        ++bad;
+      }
+    }
+    __syncthreads();
+    // reserve each slice's run, then turn the counts into batch offsets
+    for (int i = t; i < ns; i += 512)
+      if (s_cnt[i]) s_base[i] = atomicAdd(&cursor[i], s_cnt[i]);
+    __syncthreads();
+    block_scan_1024(s_cnt, s_cnt, ns, s_wt);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (w0[u] != 0xffffffffu) s_buf[s_cnt[w0[u] >> kSliceLog] + lpos[u]] = make_uint2(w0[u], w1[u]);
+    __syncthreads();
+    const uint32_t m = s_cnt[ns];
+    for (uint32_t i = t; i < m; i += 512) {
+      const uint2 e = s_buf[i];
+      const uint32_t sl = e.x >> kSliceLog;
+      pairs[(int64_t)s_start[sl] + s_base[sl] + (i - s_cnt[sl])] = e;
+    }
+    __syncthreads();
+  }
+  if (bad && err) atomicAdd(err, bad);
+}
+
+template <typename T, int OP, bool KEYS, bool CNT, bool PAIR>
+__global__ void __launch_bounds__(512)
+bin_reduce_kernel(const uint2* __restrict__ pairs, const uint32_t* __restrict__ tot, int ns,
+                  int64_t span, uint32_t* __restrict__ next,
+                  typename Acc<T, OP, KEYS>::A* __restrict__ acc, int32_t* __restrict__ cnt) {
+  using AT = Acc<T, OP, KEYS>;
+  using A = typename AT::A;
+  constexpr bool kCnt = CNT || PAIR;
+  extern __shared__ __align__(16) uint8_t bin_smem[];
+  A* s_acc = reinterpret_cast<A*>(bin_smem);
+  int32_t* s_c = reinterpret_cast<int32_t*>(bin_smem + kSliceCells * sizeof(A));
+  __shared__ uint32_t s_start[kMaxSlices + 1];
+  __shared__ uint32_t s_seg[kMaxSlices + 1];
+  __shared__ uint32_t s_wt[16];
+  __shared__ uint32_t s_w;
+  const int t = threadIdx.x;
+  block_scan_1024(tot, s_start, ns, s_wt);
+  for (int i = t; i < ns; i += 512) s_seg[i] = (uint32_t)((tot[i] + kSeg - 1) / kSeg);
+  __syncthreads();
+  block_scan_1024(s_seg, s_seg, ns, s_wt);
+  const uint32_t nseg = s_seg[ns];
+  const A ident = AT::identity();
+  for (;;) {
+    if (t == 0) s_w = atomicAdd(next, 1u);
+    __syncthreads();
+    const uint32_t w = s_w;
+    if (w >= nseg) break;
+    // the slice holding segment w (s_seg is nondecreasing)
+    int lo = 0, hi = ns - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_seg[mid] <= w) lo = mid;
+      else hi = mid - 1;
+    }
+    const int sl = lo;
+    const int64_t e0 = (int64_t)s_start[sl] + (int64_t)(w - s_seg[sl]) * kSeg;
+    const int64_t e1 = min(e0 + kSeg, (int64_t)s_start[sl] + (int64_t)tot[sl]);
+    for (int c = t; c < kSliceCells; c += 512) {
+      s_acc[c] = ident;
+      if (kCnt) s_c[c] = 0;
+    }
+    __syncthreads();
+    int64_t e = e0 + t;
+    for (; e + 3 * 512 < e1; e += 4 * 512) {  // four pairs in flight per thread
+      uint2 pr[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) pr[u] = pairs[e + u * 512];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t c = pr[u].x & (kSliceCells - 1);
+        AT::op(&s_acc[c], acc_from_bits<A>(pr[u].y));
+        if (kCnt) atomicAdd(&s_c[c], 1);
+      }
+    }
+    for (; e < e1; e += 512) {
+      const uint2 pr = pairs[e];
+      const uint32_t c = pr.x & (kSliceCells - 1);
+      AT::op(&s_acc[c], acc_from_bits<A>(pr.y));
+      if (kCnt) atomicAdd(&s_c[c], 1);
+    }
+    __syncthreads();
+    const int64_t base = (int64_t)sl << kSliceLog;
+    for (int c = t; c < kSliceCells && base + c < span; c += 512) {
+      const A v = s_acc[c];
+      const int64_t off = base + c;
+      if constexpr (kCnt) {
+        const int32_t k = s_c[c];
+        if (k == 0) continue;
+        if constexpr (PAIR) {
+          red_pair(reinterpret_cast<float*>(acc) + 2 * off, (float)v, (float)k);
+        } else {
+          AT::op(acc + off, v);
+          atomicAdd(cnt + off, k);
+        }
+      } else {
+        if (v == ident) continue;  // an untouched cell, or a no-op merge
+        AT::op(acc + off, v);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // planning + dispatch
 // ---------------------------------------------------------------------------
 inline bool is_float(int dt) { return dt == FO_F32 || dt == FO_F16 || dt == FO_BF16; }
@@ -502,7 +753,24 @@ struct Plan {
   bool counts;   // int32 counts in scratch
   bool pair;     // interleaved float (sum, count) pairs in scratch (set per call)
   size_t acc_bytes, cnt_bytes;
+  bool binned;   // destination-binned update pass (set per call)
+  size_t bin_bytes;
 };
+
+// Workspace beyond the plan for the destination-binned path: slice totals,
+// cursors and the work counter (a 12 KiB block: 4 KiB, 4 KiB, 4 bytes), then
+// n (cell, value) pairs; 0 when the path does not apply.
+// Used for products: their atomic path is a load and a compare-and-swap loop
+// per update (0.41 ms uniform / 0.87 ms Zipf at 2^24 updates into 2^20 cells),
+// the binned passes take 0.26 / 0.60 ms.  For sum, mean, amax and amin the
+// L2's atomic units stay faster (0.12-0.19 ms against 0.24-0.46 ms binned).
+inline size_t binned_bytes(int reduce, int dtype, int64_t span, int64_t n) {
+  const bool four = dtype == FO_F32 || dtype == FO_F16 || dtype == FO_BF16 || dtype == FO_I32;
+  if (reduce != FO_PROD || !four || n < kBinMinUpdates || span <= 0 ||
+      span > (int64_t)kMaxSlices * kSliceCells)
+    return 0;
+  return kBinHeaderBytes + round256((size_t)n * 8);
+}
 
 // Float sum without self and float mean may use (sum, count) pairs; the
 // workspace covers both that layout and separate float sums + int32 counts.
@@ -562,7 +830,47 @@ int run(void* out, const void* src, const void* index, const Geo& g, const OutGe
   } else if (cnt) {
     cudaMemsetAsync(cnt, 0, pl.cnt_bytes, st);
   }
-  if (n > 0) {
+  if (n > 0 && pl.binned) {
+    // destination-binned pass: 1-D contiguous index and src (checked by the caller)
+    const int64_t span = out_span(og.shape, og.str, og.ndim);
+    const int ns = (int)((span + kSliceCells - 1) / kSliceCells);
+    char* bw = reinterpret_cast<char*>(ws) + pl.acc_bytes + pl.cnt_bytes;
+    uint32_t* tot = reinterpret_cast<uint32_t*>(bw);
+    uint32_t* cursor = tot + kMaxSlices;
+    uint32_t* next = cursor + kMaxSlices;
+    uint2* pairs = reinterpret_cast<uint2*>(bw + kBinHeaderBytes);
+    if constexpr (sizeof(A) == 4) {
+      if (cudaMemsetAsync(bw, 0, kBinHeaderBytes, st) != cudaSuccess) {
+        set_error("scatter_reduce: cudaMemsetAsync failed");
+        return FO_ECUDA;
+      }
+      bin_count_kernel<I><<<sms * 4, 512, 0, st>>>((const I*)index, n, g.out_dim, g.ostr[0], ns,
+                                                   tot);
+      if (int rc = check_launch("bin_count_kernel")) return rc;
+      int64_t gb = (n + kBinBatch - 1) / kBinBatch;
+      if (gb > (int64_t)sms * 4) gb = (int64_t)sms * 4;
+      bin_pairs_kernel<T, I, OP, KEYS><<<(unsigned)gb, 512, 0, st>>>(
+          (const T*)src, (const I*)index, n, g.out_dim, g.ostr[0], ns, tot, cursor, pairs, err);
+      if (int rc = check_launch("bin_pairs_kernel")) return rc;
+      const bool with_cnt = (cnt != nullptr) || (kPairable && pl.pair);
+      const int smem = (int)(kSliceCells * sizeof(A)) + (with_cnt ? kSliceCells * 4 : 0);
+#define FO_BIN_REDUCE(C, P)                                                                    \
+  {                                                                                            \
+    auto rk = bin_reduce_kernel<T, OP, KEYS, C, P>;                                            \
+    if (cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=         \
+        cudaSuccess) {                                                                         \
+      set_error("scatter_reduce: cannot reserve %d bytes of shared memory", smem);            \
+      return FO_ECUDA;                                                                         \
+    }                                                                                          \
+    rk<<<sms * 3, 512, smem, st>>>(pairs, tot, ns, span, next, acc, cnt);                      \
+  }
+      if (kPairable && pl.pair) FO_BIN_REDUCE(false, kPairable)
+      else if (cnt) FO_BIN_REDUCE(true, false)
+      else FO_BIN_REDUCE(false, false)
+#undef FO_BIN_REDUCE
+      if (int rc = check_launch("bin_reduce_kernel")) return rc;
+    }
+  } else if (n > 0) {
     const int64_t span = out_span(og.shape, og.str, og.ndim);
     const bool use_cache = span < (int64_t)0xffffffffLL;
     int64_t grid = (n + (int64_t)kThreads * 16 - 1) / ((int64_t)kThreads * 16);
@@ -722,6 +1030,14 @@ int prepare_scatter(const void* out, const void* src, const void* index, int ndi
 }  // namespace
 }  // namespace fo
 
+extern "C" int fo_scatter_reduce_binned_bytes(int64_t out_span, int64_t n, int reduce, int dtype,
+                                              int64_t* bytes) {
+  clear_error();
+  FO_CHECK_ARG(bytes && out_span >= 0 && n >= 0, "fo_scatter_reduce_binned_bytes: bad argument");
+  *bytes = (int64_t)binned_bytes(reduce, dtype, out_span, n);
+  return FO_OK;
+}
+
 extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, int ndim,
                                  const int64_t* index_shape, const int64_t* index_strides,
                                  const int64_t* src_strides, const int64_t* out_shape,
@@ -745,6 +1061,12 @@ extern "C" int fo_scatter_reduce(void* out, const void* src, const void* index, 
               (long long)(pl.acc_bytes + pl.cnt_bytes), (long long)ws_bytes);
     return FO_EWORKSPACE;
   }
+  // the destination-binned pass when it applies and the caller's workspace
+  // holds its pairs (fo_scatter_reduce_binned_bytes); else per-update atomics
+  pl.bin_bytes = binned_bytes(reduce, dtype, span, n);
+  pl.binned = pl.bin_bytes > 0 && ndim == 1 && g.istr[0] == 1 && g.sstr[0] == 1 && workspace &&
+              aligned16(workspace) &&
+              ws_bytes >= (int64_t)(pl.acc_bytes + pl.cnt_bytes + pl.bin_bytes);
   cudaStream_t st = as_stream(stream);
   if (index_dtype == FO_I64)
     return dispatch_dtype<int64_t>(dtype, reduce, out, src, index, g, og, n, include_self != 0, pl,

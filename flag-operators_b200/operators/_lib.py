@@ -44,6 +44,7 @@ _SIGS = {
     "fo_median_all_workspace_bytes": [_i64, _i64p],
     "fo_median_all": [_c_void_p, _c_void_p, _i64, _int, _c_void_p, _i64, _c_void_p],
     "fo_scatter_reduce_workspace_bytes": [_i64, _int, _int, _int, _i64p],
+    "fo_scatter_reduce_binned_bytes": [_i64, _i64, _int, _int, _i64p],
     "fo_scatter_reduce": [_c_void_p, _c_void_p, _c_void_p, _int, _i64p, _i64p, _i64p, _i64p,
                           _i64p, _int, _int, _int, _int, _int, _c_void_p, _i64, _c_void_p,
                           _c_void_p],

@@ -10,7 +10,8 @@ toward -inf, amax/amin propagate NaN.  1-4-D tensors, any strides, reduce in
 {sum, prod, mean, amax, amin}; dtypes float32/float16/bfloat16/int32/int64.
 
 Kernels: csrc/scatter_reduce.cu (entry point fo_scatter_reduce).  Scratch
-(accumulator, counts) is allocated here with torch and passed in.
+(accumulator, counts, and for many 1-D updates the destination-binned pass's
+(cell, value) pairs) is allocated here with torch and passed in.
 Indices outside [0, self.size(dim)) are skipped on the device and counted;
 set FLAGOPS_CHECK_INDEX=1 to make the call synchronise and raise, as torch's
 CPU path does.
@@ -68,7 +69,15 @@ def _launch(out: torch.Tensor, dim: int, index: torch.Tensor, src: torch.Tensor,
     span = 1 + sum((s - 1) * st for s, st in zip(out_v.shape, out_v.stride()))
     _lib.call("fo_scatter_reduce_workspace_bytes", span, code, int(include_self), dt,
               _lib.ctypes.byref(ws_bytes))
-    ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=out.device)
+    total = ws_bytes.value
+    if ndim == 1 and index_v.stride(0) == 1 and src_v.stride(0) == 1:
+        # room for the destination-binned pass (many updates into a bounded output)
+        bin_bytes = _lib.ctypes.c_int64(0)
+        _lib.call("fo_scatter_reduce_binned_bytes", span, index_v.numel(), code, dt,
+                  _lib.ctypes.byref(bin_bytes))
+        total += bin_bytes.value
+    ws = torch.empty(max(total, 1), dtype=torch.uint8, device=out.device)
+    ws_bytes = _lib.ctypes.c_int64(total)
     err = torch.zeros(1, dtype=torch.int32, device=out.device) if _CHECK else None
     _lib.call("fo_scatter_reduce", _lib.ptr(out_v), _lib.ptr(src_v), _lib.ptr(index_v), ndim,
               _lib.i64_array(index_v.shape), _lib.i64_array(index_v.stride()),

@@ -134,6 +134,16 @@ FO_API int fo_median_all(const void* x, void* value, int64_t n, int dtype,
 FO_API int fo_scatter_reduce_workspace_bytes(int64_t out_numel, int reduce,
                                       int include_self, int dtype,
                                       int64_t* bytes);
+/*
+ * Extra workspace (bytes, appended after fo_scatter_reduce_workspace_bytes')
+ * that lets fo_scatter_reduce use its destination-binned pass for n updates
+ * into an output spanning out_span elements: 0 when that pass does not apply.
+ * The pass runs when ndim == 1, index and src are contiguous and ws_bytes
+ * covers both parts; otherwise every update is an atomic.  Replaces the same
+ * launcher as fo_scatter_reduce (operators/scatter_reduce.py:327-375).
+ */
+FO_API int fo_scatter_reduce_binned_bytes(int64_t out_span, int64_t n, int reduce, int dtype,
+                                          int64_t* bytes);
 FO_API int fo_scatter_reduce(void* out, const void* src, const void* index, int ndim,
                       const int64_t* index_shape, const int64_t* index_strides,
                       const int64_t* src_strides, const int64_t* out_shape,

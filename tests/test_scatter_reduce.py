@@ -242,3 +242,53 @@ def test_empty_index_and_cpu_rejected():
     with pytest.raises(AssertionError, match="Unsupported reduce"):
         scatter_reduce(inp, 0, torch.zeros(1, dtype=torch.long, device=DEV),
                        torch.zeros(1, device=DEV), "median")
+
+
+@pytest.mark.parametrize("reduce", REDUCES)
+@pytest.mark.parametrize("include_self", [True, False])
+def test_binned_path_edges(reduce, include_self):
+    """The destination-binned pass (1-D contiguous updates, n >= 2^20): a length
+    that is not a multiple of 4, slices left empty, a hot cell, signed values
+    around 1 for products, NaN in amax/amin, a strided (span 2x) output, and
+    int32 sums and means (bit-exact)."""
+    g = torch.Generator().manual_seed(41)
+    n = (1 << 20) + 3
+    n_out = 50000
+    idx = torch.randint(0, n_out, (n,), generator=g)
+    idx[idx % 7 == 3] = 17                      # a hot cell
+    idx[(idx >= 30000) & (idx < 38192)] = 5     # one slice never reached
+    src = 1.0 + 0.01 * torch.randn(n, generator=g)
+    src[::1001] *= -1.0
+    if reduce in ("amax", "amin"):
+        src[12345] = float("nan")
+    inp = torch.randn(n_out, generator=g)
+    _check(inp, 0, idx, src, reduce, include_self=include_self, variant="out")
+    _check(inp, 0, idx, src, reduce, include_self=include_self, variant="inplace")
+    # in place into a strided view (the output spans twice its cells)
+    ref = oracle.scatter_reduce(inp, 0, idx, src, reduce, include_self=include_self)
+    buf = torch.zeros(2 * n_out, device=DEV)
+    view = buf[::2]
+    view.copy_(inp.to(DEV))
+    scatter_reduce_(view, 0, idx.to(DEV), src.to(DEV), reduce, include_self=include_self)
+    _compare(view, ref, reduce, inp, 0, idx, src, include_self)
+    assert bool((buf[1::2] == 0).all()), "cells between the view's elements were written"
+    if reduce in ("sum", "mean"):
+        inp_i = torch.randint(-50, 50, (n_out,), generator=g, dtype=torch.int32)
+        src_i = torch.randint(-100, 100, (n,), generator=g, dtype=torch.int32)
+        _check(inp_i, 0, idx, src_i, reduce, include_self=include_self)
+
+
+def test_binned_path_out_of_range_indices_are_skipped():
+    import operators.scatter_reduce as sr
+    g = torch.Generator().manual_seed(42)
+    n = 1 << 20
+    idx = torch.randint(0, 1000, (n,), generator=g)
+    bad = torch.rand(n, generator=g) < 0.01
+    idx[bad] = 5000                              # outside [0, 1000)
+    src = torch.randn(n, generator=g)
+    inp = torch.zeros(1000)
+    ref = oracle.scatter_reduce(inp, 0, idx[~bad], src[~bad], "sum")
+    got = scatter_reduce(inp.to(DEV), 0, idx.to(DEV), src.to(DEV), "sum")
+    _compare(got, ref, "sum", inp, 0, idx[~bad], src[~bad], True)
+    if sr._CHECK:
+        pytest.skip("index checking raises instead")
