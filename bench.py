@@ -519,6 +519,10 @@ def _delta_close(got, ref, rtol=2e-2):
     return ok, f"max err {err.max().item():.3e} (rms {rms:.3e})"
 
 
+SHARDED_LINES = ("rms_norm_bf16_rows", "median_a_rows", "ce_rows_sharded", "ce_vocab_sharded",
+                 "delta_heads")
+
+
 def run_sharded(args, dev, peaks, traffic, dist):
     """Each workload of the target spec split over the ranks (strong scaling):
     rms_norm and median rows, cross-entropy rows and vocabulary columns, delta
@@ -743,10 +747,18 @@ def main():
         return
 
     dist = None
-    if world > 1:
+    sharded_only = bool(args.only) and args.only.startswith(SHARDED_LINES)
+    if world > 1 or sharded_only:
+        # --only <a sharded line> on one GPU runs that line with a single-rank
+        # group (its kernels in one process, e.g. for a profiler capture)
         import torch.distributed as dist_mod
         torch.cuda.set_device(local)
         import datetime
+        if world == 1:
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29561")
+            os.environ.setdefault("RANK", "0")
+            os.environ.setdefault("WORLD_SIZE", "1")
         dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", local))
         dist = dist_mod
@@ -762,7 +774,7 @@ def main():
 
     if args.only:
         do_cpu = (rank == 0 and world == 1)
-        per_op = run_per_op(args, dev, peaks, traffic, do_cpu, dist)
+        per_op = {} if sharded_only else run_per_op(args, dev, peaks, traffic, do_cpu, dist)
         if dist is not None:
             per_op.update(run_sharded(args, dev, peaks, traffic, dist))
         clocks = sampler.stop()

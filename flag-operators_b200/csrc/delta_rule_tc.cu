@@ -697,9 +697,11 @@ constexpr uint32_t TI_K = 0;         // fp16 2 x [128 x 128B]: rows 0-63 K, rows
                                      // so K K^T lands in all four TMEM lane quadrants
 constexpr uint32_t TI_OUT = 32768;   // fp16 T tile [64 x 128B]
 constexpr uint32_t TI_A = 40960;     // fp32 [64][68]: N = -A stored transposed
-constexpr uint32_t TI_TSC = 58368;   // fp32 [2][32][32]: T00 | T11
-constexpr uint32_t TI_G = 66560;     // lc, z, neg, signed beta: 64 each
-constexpr uint32_t TI_BAR = 67584;   // mbarrier, TMEM address
+constexpr uint32_t TI_TSC = 58368;   // fp32 [64][kTscStride]: T00 (rows 0-31) | T11 (rows 32-63)
+constexpr int kTscStride = 36;       // 144-byte rows: 16-byte aligned, and the 8 rows a warp reads
+                                     // in T10 = T11 P start on 8 different banks
+constexpr uint32_t TI_G = 67584;     // lc, z, neg, signed beta: 64 each
+constexpr uint32_t TI_BAR = 68608;   // mbarrier, TMEM address
 constexpr uint32_t kTiSmem = TI_BAR + 64 + 1024;  // + alignment slack
 constexpr uint32_t kTiCols = 64;
 
@@ -872,7 +874,7 @@ gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __
 #pragma unroll
       for (int a = 0; a < 32; ++a) {
         const float tv = (a & 1) ? col[a / 2].y : col[a / 2].x;
-        Tsc[(32 * I + a) * 32 + cc] = tv;
+        Tsc[(32 * I + a) * kTscStride + cc] = tv;
         *reinterpret_cast<__half*>(sm + TI_OUT + tc::sw128_off(32 * I + a, p)) = __float2half_rn(tv);
         if (I == 1)
           *reinterpret_cast<__half*>(sm + TI_OUT + tc::sw128_off(a, p)) = __float2half_rn(0.f);
@@ -887,8 +889,8 @@ gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __
       for (int d = 0; d < 32; ++d) {
         const float n = sA[d * kAStride + 32 + a];
         const float2 n2 = make_float2(n, n);
-        const float4 t0 = *reinterpret_cast<const float4*>(Tsc + d * 32 + b0);
-        const float4 t1 = *reinterpret_cast<const float4*>(Tsc + d * 32 + b0 + 4);
+        const float4 t0 = *reinterpret_cast<const float4*>(Tsc + d * kTscStride + b0);
+        const float4 t1 = *reinterpret_cast<const float4*>(Tsc + d * kTscStride + b0 + 4);
         acc[0] = fma2(n2, make_float2(t0.x, t0.y), acc[0]);
         acc[1] = fma2(n2, make_float2(t0.z, t0.w), acc[1]);
         acc[2] = fma2(n2, make_float2(t1.x, t1.y), acc[2]);
@@ -905,7 +907,7 @@ gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __
       float2 acc[4] = {};
 #pragma unroll
       for (int c2 = 0; c2 < 32; ++c2) {
-        const float tv = Tsc[(32 + a) * 32 + c2];
+        const float tv = Tsc[(32 + a) * kTscStride + c2];
         const float2 t2 = make_float2(tv, tv);
         const float4 p0 = *reinterpret_cast<const float4*>(sA + (32 + c2) * kAStride + b0);
         const float4 p1 = *reinterpret_cast<const float4*>(sA + (32 + c2) * kAStride + b0 + 4);

@@ -90,13 +90,13 @@ def test_tensor_core_dtypes_and_fp32_gates(dtype):
 
 
 def test_baseline_config():
-    """B=8, H=16, L=8192, D=128 bf16: two heads against the oracle, all heads
-    against the independent per-step CUDA kernel (fp32 state)."""
+    """B=8, H=16, L=8192, D=128 bf16: five heads spread over the batch against the
+    oracle, all heads against the independent per-step CUDA kernel (fp32 state)."""
     B, H, L, D = 8, 16, 8192, 128
     ins = _make(B, H, L, D, seed=3)
     dins = [t.to(DEV) for t in ins]
     o, h = chunk_gated_delta_rule(*dins, output_final_state=True)
-    sel = [(0, 0), (7, 15)]
+    sel = [(0, 0), (1, 5), (3, 9), (5, 2), (7, 15)]
     for b, hh in sel:
         sub = [t[b:b + 1, hh:hh + 1] for t in ins]
         ro, rh = oracle.delta_rule_forward(*sub, output_final_state=True)
