@@ -652,10 +652,16 @@ def run_sharded(args, dev, peaks, traffic, dist):
                 ok = bool(torch.allclose(grad[sample.to(dev)].float().cpu(), gs[:, c0:c1],
                                          rtol=2e-2, atol=2e-5 * float(gs.abs().max())))
                 det = det if ok else f"rank {rank} gradient block differs"
+            from operators import fused_cross_entropy as fce
+            fused = isinstance(fce._PEER.get((id(dist.group.WORLD), dev.index)),
+                               fce._PeerRegions)
             res["ce_vocab_sharded"] = line(
-                "ce_vocab_sharded", nbytes, ms, 5, _agree(dist, ok, det),
+                "ce_vocab_sharded", nbytes, ms, 3 if fused else 5, _agree(dist, ok, det),
                 {"shard": f"columns [{c0}, {c1}) of {V}, all rows",
-                 "collective": "all_gather of per-row (max, sum-exp, target logit, row sum)",
+                 "collective": ("per-row (max, sum-exp, target logit, row sum) stored into every "
+                                "rank's region over NVLink peer memory inside the fused kernel "
+                                "(fo_ce_shard_p2p_fwd)") if fused else
+                               "all_gather of per-row (max, sum-exp, target logit, row sum)",
                  "note": "algorithmic bytes = one read of the logits + one write of dlogits"})
             del lsh, grad
         del lg

@@ -498,6 +498,181 @@ int ce_bwd_t(const void* logits, const int64_t* target, const float* lse, const 
   return check_launch("ce_bwd_kernel");
 }
 
+
+// ---------------------------------------------------------------------------
+// Vocabulary-sharded forward (+ gradient) as one kernel over NVLink peer memory
+// ---------------------------------------------------------------------------
+// Each rank owns a region of the same layout, mapped into every other rank's
+// address space (CUDA IPC); capacity Bc rows:
+//   stats [2][P][Bc] float4   (max, sum exp(x - max), target logit or 0, row sum)
+//                              of source rank p for row b, double-buffered by
+//                              the call's epoch parity
+//   flags [P][Bc] uint32       epoch of the call whose stats of (p, b) landed
+// A CTA computes the statistics of its row (the row stays in L2: evict_last),
+// stores them into every rank's region (P2P stores) and publishes each with a
+// system-scope release store of the epoch into that rank's flag.  `lag` rows
+// later (0 or 1) it acquires the P flags of that row in its own region,
+// combines the statistics in rank order (the same result on every rank) and
+// writes that row's gradient slice, re-reading the row from L2.  Forward +
+// gradient cost one HBM read and one write of the rank's [B, V_local] block.
+// With lag 1 the exchange (16 bytes per row and rank) overlaps the next row's
+// statistics, at the price of two rows per CTA held in L2; the host picks lag 1
+// when that fits (short rows, many ranks), else lag 0, where the other CTAs of
+// the SM cover the wait.
+// Ranks run the same persistent grid over the same rows, so a CTA waits only on
+// rows its counterparts on the other GPUs process at the same time.  Waits are
+// bounded: one that runs out counts in g_ce_p2p_timeouts, marks the epoch as
+// failed (every later wait of the call gives up at once) and leaves that row's
+// loss NaN.  Parity double-buffering keeps a rank that starts call k + 1 from
+// overwriting statistics a slower rank still reads in call k (a rank cannot get
+// two calls ahead: call k + 1 needs every rank's call-(k + 1) statistics).
+__device__ unsigned int g_ce_p2p_timeouts;
+__device__ unsigned int g_ce_p2p_failed_epoch;
+constexpr uint32_t kP2PWaitLimit = 1u << 22;
+constexpr int kP2PMaxRanks = 8;
+
+struct PeerRegions {
+  void* r[kP2PMaxRanks];
+};
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr int kP2PThreads = 256;  // 4 CTAs per SM: the shard rows are short
+
+template <typename T, bool LS>
+__global__ void __launch_bounds__(kP2PThreads)
+ce_shard_p2p_kernel(const T* __restrict__ logits, const int64_t* __restrict__ target,
+                    float* __restrict__ loss_rows, float* __restrict__ lse_out,
+                    T* __restrict__ dlogits, const float* __restrict__ n_valid, int64_t B,
+                    int64_t Vn, int64_t ld, int64_t col0, int64_t V, int64_t ignore_index,
+                    float eps, int reduction, PeerRegions peers, int P, int rank, int64_t Bc,
+                    uint32_t epoch, int lag) {
+  __shared__ float sm[96];
+  __shared__ float4 s_st[kP2PMaxRanks];
+  __shared__ int s_bad;
+  const bool grad = dlogits != nullptr;
+  const int par = (int)(epoch & 1u);
+  const int64_t G = gridDim.x;
+  const int64_t nmine = B > (int64_t)blockIdx.x ? (B - 1 - blockIdx.x) / G + 1 : 0;
+  float4* own_stats = reinterpret_cast<float4*>(peers.r[rank]);
+  const uint32_t* own_flags =
+      reinterpret_cast<const uint32_t*>(own_stats + 2 * (int64_t)P * Bc);
+  for (int64_t j = 0; j < nmine + lag; ++j) {
+    if (j < nmine) {
+      // ---- statistics of row j, published to every rank
+      const int64_t b = blockIdx.x + j * G;
+      const T* row = logits + b * ld;
+      MS st{-INFINITY, 0.f};
+      float rsum = 0.f;
+      l2_prefetch(row, Vn * (int64_t)sizeof(T));
+      row_stats<T>(row, Vn, LS, grad, st, rsum);
+      block_ms(st, rsum, sm);
+      if (threadIdx.x < P) {
+        const int q = threadIdx.x;
+        const int64_t t = target[b];
+        float xt = 0.f;
+        if (t != ignore_index && t >= col0 && t < col0 + Vn) xt = to_f<T>(row[t - col0]);
+        float4* qs = reinterpret_cast<float4*>(peers.r[q]);
+        uint32_t* qf = reinterpret_cast<uint32_t*>(qs + 2 * (int64_t)P * Bc);
+        qs[((int64_t)par * P + rank) * Bc + b] = make_float4(st.m, st.s, xt, rsum);
+        st_release_sys_u32(qf + (int64_t)rank * Bc + b, epoch);
+      }
+    }
+    if (j >= lag) {
+      // ---- row j - lag: every rank's statistics, combine, gradient slice
+      const int64_t b = blockIdx.x + (j - lag) * G;
+      if (threadIdx.x == 0) s_bad = 0;
+      __syncthreads();
+      if (threadIdx.x < P) {
+        const int p = threadIdx.x;
+        const uint32_t* f = own_flags + (int64_t)p * Bc + b;
+        bool ok = true;
+        for (uint32_t n = 0; ld_acquire_sys_u32(f) != epoch; ++n) {
+          if (n >= kP2PWaitLimit || *reinterpret_cast<volatile uint32_t*>(&g_ce_p2p_failed_epoch) ==
+                                        epoch) {
+            ok = false;
+            break;
+          }
+        }
+        if (ok) {
+          s_st[p] = __ldcg(own_stats + ((int64_t)par * P + p) * Bc + b);
+        } else {
+          if (atomicExch(&g_ce_p2p_failed_epoch, epoch) != epoch) atomicAdd(&g_ce_p2p_timeouts, 1u);
+          s_bad = 1;
+        }
+      }
+      __syncthreads();
+      MS st{-INFINITY, 0.f};
+      float xt = 0.f, rsum = 0.f;
+      for (int p = 0; p < P; ++p) {
+        const float4 v = s_st[p];
+        st = ms_merge(st, MS{v.x, v.y});
+        xt += v.z;
+        rsum += v.w;
+      }
+      const float lse = s_bad ? NAN : st.m + logf(st.s);
+      const int64_t t = target[b];
+      const bool valid = (t != ignore_index);
+      if (threadIdx.x == 0) {
+        float loss = 0.f;
+        if (valid) {
+          loss = (t >= 0 && t < V) ? lse - (1.f - eps) * xt : NAN;
+          if (LS) loss -= eps * (rsum / (float)V);
+        }
+        loss_rows[b] = s_bad ? NAN : loss;
+        lse_out[b] = lse;
+      }
+      if (grad) {
+        float scale = valid ? 1.f : 0.f;
+        if (valid && reduction == FO_RED_MEAN) scale = 1.f / *n_valid;
+        const T* row = logits + b * ld;
+        row_grad<T>(row, dlogits + b * Vn, Vn, col0, t, lse, scale, LS ? eps / (float)V : 0.f,
+                    1.f - eps);
+        fix_target<T>(row, dlogits + b * Vn, Vn, col0, t, lse, scale, LS ? eps / (float)V : 0.f,
+                      1.f - eps);
+      }
+      __syncthreads();  // s_st / s_bad are rewritten for the next row
+    }
+  }
+}
+
+template <typename T>
+int ce_shard_p2p_t(const void* logits, const int64_t* target, float* loss_rows, float* lse,
+                   float* out_scalar, float* n_valid, void* dlogits, int64_t B, int64_t Vn,
+                   int64_t ld, int64_t col0, int64_t V, int64_t ignore_index, float eps,
+                   int reduction, const PeerRegions& peers, int P, int rank, int64_t Bc,
+                   uint32_t epoch, cudaStream_t st) {
+  ce_count_valid_kernel<<<1, 1024, 0, st>>>(target, B, ignore_index, n_valid);
+  if (int rc = check_launch("ce_count_valid_kernel")) return rc;
+  // every CTA resident at once (a CTA waits only on its counterparts on other
+  // GPUs, which run the same grid); rows held in L2 (grid x (1 + lag) rows,
+  // evict_last) kept under ~72 MB of the 126 MB
+  auto kern = eps != 0.f ? ce_shard_p2p_kernel<T, true> : ce_shard_p2p_kernel<T, false>;
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kP2PThreads, 0);
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 4) per_sm = 4;
+  const int grid = grid_rows(B, per_sm);
+  const double row_bytes = (double)Vn * sizeof(T);
+  const int lag = (dlogits && (double)grid * 2.0 * row_bytes <= 72.0 * (1 << 20)) ? 1 : 0;
+  kern<<<grid, kP2PThreads, 0, st>>>((const T*)logits, target, loss_rows, lse, (T*)dlogits,
+                                     n_valid, B, Vn, ld, col0, V, ignore_index, eps, reduction,
+                                     peers, P, rank, Bc, epoch, lag);
+  if (int rc = check_launch("ce_shard_p2p_kernel")) return rc;
+  if (reduction != FO_RED_NONE) {
+    ce_reduce_kernel<<<1, 1024, 0, st>>>(loss_rows, B, n_valid, reduction, out_scalar);
+    return check_launch("ce_reduce_kernel");
+  }
+  return FO_OK;
+}
+
 int check_common(const void* logits, const void* target, int64_t B, int64_t V, int64_t ld,
                  int dtype, const char* op) {
   FO_CHECK_ARG(B >= 0 && V > 0 && ld >= V, "%s: bad shape B=%lld V=%lld ld=%lld", op,
@@ -743,4 +918,67 @@ extern "C" int fo_ce_count_valid(const int64_t* target, int64_t B, int64_t ignor
   FO_CHECK_ARG(B >= 0 && n_valid_out && (B == 0 || target), "fo_ce_count_valid: bad argument");
   ce_count_valid_kernel<<<1, 1024, 0, as_stream(stream)>>>(target, B, ignore_index, n_valid_out);
   return check_launch("ce_count_valid_kernel");
+}
+
+extern "C" int fo_ce_shard_p2p_region_bytes(int P, int64_t rows, int64_t* bytes) {
+  clear_error();
+  FO_CHECK_ARG(bytes && P >= 1 && P <= kP2PMaxRanks && rows >= 0,
+               "fo_ce_shard_p2p_region_bytes: bad argument (1 <= P <= %d)", kP2PMaxRanks);
+  *bytes = 2 * (int64_t)P * rows * 16 + (int64_t)P * rows * 4;
+  return FO_OK;
+}
+
+extern "C" int fo_ce_shard_p2p_fwd(const void* logits, const int64_t* target, float* loss_rows,
+                                   float* lse, float* out_scalar, float* n_valid_out,
+                                   void* dlogits, int64_t B, int64_t V_local, int64_t ld,
+                                   int64_t v_offset, int64_t V, int64_t ignore_index,
+                                   float label_smoothing, int reduction, int dtype,
+                                   void* const* regions, int P, int rank, int64_t rows_cap,
+                                   uint32_t epoch, void* stream) {
+  clear_error();
+  if (int rc = check_common(logits, target, B, V_local, ld, dtype, "fo_ce_shard_p2p_fwd"))
+    return rc;
+  FO_CHECK_ARG(P >= 2 && P <= kP2PMaxRanks && rank >= 0 && rank < P && regions,
+               "fo_ce_shard_p2p_fwd: bad rank layout (P=%d rank=%d)", P, rank);
+  FO_CHECK_ARG(B <= rows_cap, "fo_ce_shard_p2p_fwd: %lld rows exceed the regions' %lld",
+               (long long)B, (long long)rows_cap);
+  FO_CHECK_ARG(epoch != 0u, "fo_ce_shard_p2p_fwd: epoch 0 is the regions' initial state");
+  FO_CHECK_ARG(v_offset >= 0 && v_offset + V_local <= V, "fo_ce_shard_p2p_fwd: bad v_offset");
+  FO_CHECK_ARG(loss_rows && lse && n_valid_out && (reduction == FO_RED_NONE || out_scalar),
+               "fo_ce_shard_p2p_fwd: null pointer");
+  PeerRegions peers{};
+  for (int p = 0; p < P; ++p) {
+    FO_CHECK_ARG(regions[p], "fo_ce_shard_p2p_fwd: null region of rank %d", p);
+    FO_CHECK_ARG((reinterpret_cast<uintptr_t>(regions[p]) & 15) == 0,
+                 "fo_ce_shard_p2p_fwd: region of rank %d not 16-byte aligned", p);
+    peers.r[p] = regions[p];
+  }
+  if (B == 0) return FO_OK;
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case FO_F32:
+      return ce_shard_p2p_t<float>(logits, target, loss_rows, lse, out_scalar, n_valid_out,
+                                   dlogits, B, V_local, ld, v_offset, V, ignore_index,
+                                   label_smoothing, reduction, peers, P, rank, rows_cap, epoch, st);
+    case FO_F16:
+      return ce_shard_p2p_t<__half>(logits, target, loss_rows, lse, out_scalar, n_valid_out,
+                                    dlogits, B, V_local, ld, v_offset, V, ignore_index,
+                                    label_smoothing, reduction, peers, P, rank, rows_cap, epoch,
+                                    st);
+    default:
+      return ce_shard_p2p_t<__nv_bfloat16>(logits, target, loss_rows, lse, out_scalar,
+                                           n_valid_out, dlogits, B, V_local, ld, v_offset, V,
+                                           ignore_index, label_smoothing, reduction, peers, P,
+                                           rank, rows_cap, epoch, st);
+  }
+}
+
+extern "C" int fo_ce_p2p_timeouts(unsigned int* count) {
+  clear_error();
+  FO_CHECK_ARG(count, "fo_ce_p2p_timeouts: null pointer");
+  if (cudaMemcpyFromSymbol(count, g_ce_p2p_timeouts, sizeof(unsigned int)) != cudaSuccess) {
+    set_error("fo_ce_p2p_timeouts: cannot read the device counter");
+    return FO_ECUDA;
+  }
+  return FO_OK;
 }

@@ -65,6 +65,15 @@ _SIGS = {
                         _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _int, _int,
                         _c_void_p],
     "fo_ce_count_valid": [_c_void_p, _i64, _i64, _c_void_p, _c_void_p],
+    "fo_ce_shard_p2p_region_bytes": [_int, _i64, _i64p],
+    "fo_ce_shard_p2p_fwd": [_c_void_p] * 7 + [_i64, _i64, _i64, _i64, _i64, _i64, _f32, _int,
+                                              _int, _c_void_p, _int, _int, _i64, ctypes.c_uint32,
+                                              _c_void_p],
+    "fo_ce_p2p_timeouts": [_c_void_p],
+    "fo_peer_export": [_c_void_p, _c_void_p, _i64p],
+    "fo_peer_open": [_c_void_p, _i64, ctypes.POINTER(ctypes.c_void_p)],
+    "fo_peer_close": [_c_void_p, _i64],
+    "fo_peer_can_access": [_int, _int, ctypes.POINTER(ctypes.c_int)],
     "fo_ce_rows_fwd": [_c_void_p] * 7 + [_i64, _i64, _i64, _i64, _f32, _int, _int, _c_void_p],
     "fo_gdr_workspace_bytes": [_i64, _i64, _i64, _i64, _int, _i64p],
     "fo_gdr_fwd": [_c_void_p] * 8 + [_i64, _i64, _i64, _i64, _int, _int, _c_void_p, _i64,
@@ -99,6 +108,8 @@ def load() -> ctypes.CDLL:
         lib.fo_last_error.restype = ctypes.c_char_p
         lib.fo_last_error.argtypes = []
         lib.fo_abi_version.restype = ctypes.c_int
+        lib.fo_peer_handle_bytes.restype = ctypes.c_int
+        lib.fo_peer_handle_bytes.argtypes = []
         for name, args in _SIGS.items():
             fn = getattr(lib, name, None)
             if fn is None:
@@ -110,7 +121,7 @@ def load() -> ctypes.CDLL:
 
 
 def declared_symbols() -> list[str]:
-    return ["fo_last_error", "fo_abi_version", *_SIGS.keys()]
+    return ["fo_last_error", "fo_abi_version", "fo_peer_handle_bytes", *_SIGS.keys()]
 
 
 def call(name: str, *args) -> None:

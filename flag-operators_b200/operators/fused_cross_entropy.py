@@ -22,6 +22,7 @@ one-float all-reduces (the valid-row count before the kernel, the loss sum after
 """
 from __future__ import annotations
 
+import ctypes
 import logging
 
 import torch
@@ -97,8 +98,106 @@ class _FusedCrossEntropy(torch.autograd.Function):
         return dlogits, None, None, None, None
 
 
+class _PeerRegions:
+    """The NVLink exchange regions of one process group on this rank's device.
+
+    Every rank allocates one region (fo_ce_shard_p2p_region_bytes), zeroes it
+    and exports it as a CUDA IPC handle; the handles are exchanged once over
+    the group and each rank maps the other ranks' regions, so the fused kernel
+    stores its per-row statistics straight into every rank's region.  The
+    regions grow (re-exchanged) when a call has more rows than they hold.
+    """
+
+    def __init__(self, group, dev, rows):
+        import torch.distributed as dist
+        self.group, self.dev = group, dev
+        self.P, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.cap = int(rows)
+        nbytes = ctypes.c_int64()
+        _lib.call("fo_ce_shard_p2p_region_bytes", self.P, self.cap, ctypes.byref(nbytes))
+        self.region = torch.zeros(nbytes.value, dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize(dev)  # zeroed before any peer can map and write it
+        hb = _lib.load().fo_peer_handle_bytes()
+        handle = (ctypes.c_uint8 * hb)()
+        off = ctypes.c_int64()
+        _lib.call("fo_peer_export", _lib.ptr(self.region), handle, ctypes.byref(off))
+        entries = [None] * self.P
+        dist.all_gather_object(entries, (bytes(handle), off.value), group=group)
+        self.ptrs, self.opened = [], []
+        for p, (h, o) in enumerate(entries):
+            if p == self.rank:
+                self.ptrs.append(self.region.data_ptr())
+                continue
+            out = ctypes.c_void_p()
+            hbuf = (ctypes.c_uint8 * hb).from_buffer_copy(h)
+            _lib.call("fo_peer_open", hbuf, o, ctypes.byref(out))
+            self.ptrs.append(out.value)
+            self.opened.append((out.value, o))
+        self.table = (ctypes.c_void_p * self.P)(*self.ptrs)
+        self.epoch = 0
+
+    def close(self):
+        torch.cuda.synchronize(self.dev)  # no kernel of this rank still uses the mappings
+        for ptr_, off in self.opened:
+            _lib.call("fo_peer_close", ctypes.c_void_p(ptr_), off)
+        self.opened = []
+
+
+_PEER = {}
+
+
+def _peer_regions(group, dev, rows):
+    """_PeerRegions of the group on dev, or None when the fused NVLink path does
+    not apply: fewer than 2 or more than 8 ranks, a backend other than NCCL, ranks
+    on more than one host or sharing a GPU, no peer access, or FLAGOPS_CE_P2P=0.
+    Every rank reaches the same decision (it is exchanged over the group)."""
+    import os
+    import socket
+    import torch.distributed as dist
+    if os.environ.get("FLAGOPS_CE_P2P", "1") == "0":
+        return None
+    key = (id(group), dev.index)
+    st = _PEER.get(key)
+    if st is False:
+        return None
+    if st is not None and st.group is group and st.cap >= rows:
+        return st
+    P = dist.get_world_size(group)
+    if st is None:
+        if not (2 <= P <= 8) or dist.get_backend(group) != "nccl":
+            _PEER[key] = False
+            return None
+        infos = [None] * P
+        dist.all_gather_object(infos, (socket.gethostname(), dev.index), group=group)
+        ok = len({h for h, _ in infos}) == 1 and len({d for _, d in infos}) == P
+        for _, d in infos if ok else ():
+            c = ctypes.c_int(0)
+            _lib.call("fo_peer_can_access", dev.index, d, ctypes.byref(c))
+            ok = ok and bool(c.value)
+        oks = [None] * P
+        dist.all_gather_object(oks, ok, group=group)
+        if not all(oks):
+            _PEER[key] = False
+            return None
+    else:
+        # more rows than the regions hold: every rank re-allocates at this call
+        # (the new regions are zeroed, so the epochs start again at 1)
+        st.close()
+    st = _PeerRegions(group, dev, max(int(rows), 1024))
+    _PEER[key] = st
+    return st
+
+
 class _ShardedCrossEntropy(torch.autograd.Function):
-    """Cross-entropy over vocabulary-sharded logits (one NCCL all-gather of row stats)."""
+    """Cross-entropy over vocabulary-sharded logits.
+
+    Ranks on distinct GPUs of one host with peer access: one fused kernel per
+    rank (fo_ce_shard_p2p_fwd) computes the row statistics, exchanges them over
+    NVLink peer memory and writes the gradient slice in the same pass (one HBM
+    read and one write of the block).  Otherwise: per-row statistics, one
+    all-gather over the group, a combine kernel, and the gradient recomputed in
+    backward.
+    """
 
     @staticmethod
     def forward(ctx, logits, target, reduction, ignore_index, label_smoothing, group, v_offset,
@@ -110,6 +209,30 @@ class _ShardedCrossEntropy(torch.autograd.Function):
         ld = logits.stride(0) if B > 1 else Vn
         target = target.to(torch.int64).contiguous()
         P = dist.get_world_size(group)
+        ctx.grad_ready = False
+        peer = _peer_regions(group, dev, B) if B > 0 else None
+        if peer is not None:
+            loss_rows = torch.empty(B, dtype=torch.float32, device=dev)
+            lse = torch.empty(B, dtype=torch.float32, device=dev)
+            scalar = torch.empty((), dtype=torch.float32, device=dev)
+            n_valid = torch.empty(1, dtype=torch.float32, device=dev)
+            want_grad = bool(ctx.needs_input_grad[0])
+            dlogits = torch.empty((B, Vn), dtype=logits.dtype, device=dev) if want_grad else None
+            peer.epoch += 1
+            _lib.call("fo_ce_shard_p2p_fwd", _lib.ptr(logits), _lib.ptr(target),
+                      _lib.ptr(loss_rows), _lib.ptr(lse), _lib.ptr(scalar), _lib.ptr(n_valid),
+                      _lib.ptr(dlogits), B, Vn, ld, v_offset, V, int(ignore_index),
+                      float(label_smoothing), _RED[reduction], _lib.dtype_code(logits.dtype),
+                      peer.table, peer.P, peer.rank, peer.cap, peer.epoch,
+                      _lib.stream_of(logits))
+            ctx.grad_ready = dlogits is not None
+            if dlogits is not None:
+                ctx.save_for_backward(logits, target, lse, n_valid, dlogits)
+            else:
+                ctx.save_for_backward(logits, target, lse, n_valid)
+            ctx.args = (reduction, int(ignore_index), float(label_smoothing), v_offset, V, ld)
+            out = loss_rows if reduction == "none" else scalar
+            return out.to(logits.dtype)
         stats = torch.empty(B, 4, dtype=torch.float32, device=dev)
         _lib.call("fo_ce_shard_stats", _lib.ptr(logits), _lib.ptr(target), _lib.ptr(stats), B,
                   Vn, ld, v_offset, int(ignore_index), _lib.dtype_code(logits.dtype),
@@ -132,11 +255,20 @@ class _ShardedCrossEntropy(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_output):
-        logits, target, lse, n_valid = ctx.saved_tensors
+        saved = ctx.saved_tensors
+        logits, target, lse, n_valid = saved[:4]
         reduction, ignore_index, ls, v_offset, V, ld = ctx.args
         B, Vn = logits.shape
         go = grad_output.contiguous()
         is_vec = 1 if (reduction == "none" and go.ndim == 1) else 0
+        if ctx.grad_ready:
+            # the fused kernel wrote the gradient for grad_output == 1
+            dlogits = saved[4]
+            ctx.grad_ready = False
+            _lib.call("fo_ce_scale_grad", _lib.ptr(dlogits), _lib.ptr(go),
+                      _lib.dtype_code(go.dtype), is_vec, B, Vn, Vn,
+                      _lib.dtype_code(dlogits.dtype), _lib.stream_of(dlogits))
+            return dlogits, None, None, None, None, None, None, None
         dlogits = torch.empty((B, Vn), dtype=logits.dtype, device=logits.device)
         _lib.call("fo_ce_shard_bwd", _lib.ptr(logits), _lib.ptr(target), _lib.ptr(lse),
                   _lib.ptr(go), _lib.dtype_code(go.dtype), is_vec, _lib.ptr(n_valid),

@@ -2,7 +2,8 @@
  * flagops.h — C ABI of the B200 (sm_100a) five-operator kernel set.
  *
  * Every entry point takes raw device pointers, int64 sizes, dtype codes and a
- * cudaStream_t passed as void*.  Nothing here allocates device memory: scratch
+ * cudaStream_t passed as void*.  Nothing here allocates device memory (only
+ * fo_peer_open maps a buffer that another process allocated): scratch
  * ("workspace") is owned by the caller, sized by the matching *_workspace_bytes
  * query.  Calls are stream-ordered and never synchronise the host.  The return
  * value is a status code (FO_OK == 0); fo_last_error() gives the message of the
@@ -256,6 +257,51 @@ FO_API int fo_ce_shard_bwd(const void* logits, const int64_t* target, const floa
                     int64_t V_local, int64_t ld, int64_t v_offset, int64_t V,
                     int64_t ignore_index, float label_smoothing, int reduction,
                     int dtype, void* stream);
+
+/*
+ * Vocabulary-sharded forward and gradient in ONE kernel that exchanges the
+ * per-row statistics over NVLink peer memory instead of a collective (no
+ * reference counterpart; the reference is single-device, and this replaces
+ * the three steps above when every rank has its own GPU with peer access).
+ * regions[p] (p < P <= 8) is rank p's region of fo_ce_shard_p2p_region_bytes(P,
+ * rows_cap) bytes, zeroed once before its first use and mapped into this
+ * process (fo_peer_open; regions[rank] is this rank's own); B <= rows_cap.
+ * Every rank calls with the same B, P, rows_cap and epoch, and epoch grows by
+ * one per call (starting at 1).  Writes loss_rows, lse, out_scalar and
+ * n_valid_out as fo_ce_fwd (the full-vocabulary loss, identical on every rank)
+ * and, when dlogits ([B, V_local], logits' dtype) is non-null, this rank's
+ * gradient slice for grad_output == 1 (complete backward with
+ * fo_ce_scale_grad).  One HBM read and one write of the rank's block.  Waits on
+ * other ranks are bounded: one that runs out is counted by fo_ce_p2p_timeouts
+ * and leaves NaN in the rows it could not complete.
+ */
+FO_API int fo_ce_shard_p2p_region_bytes(int P, int64_t rows_cap, int64_t* bytes);
+FO_API int fo_ce_shard_p2p_fwd(const void* logits, const int64_t* target, float* loss_rows,
+                               float* lse, float* out_scalar, float* n_valid_out,
+                               void* dlogits, int64_t B, int64_t V_local, int64_t ld,
+                               int64_t v_offset, int64_t V, int64_t ignore_index,
+                               float label_smoothing, int reduction, int dtype,
+                               void* const* regions, int P, int rank, int64_t rows_cap,
+                               uint32_t epoch, void* stream);
+/* Number of peer waits of fo_ce_shard_p2p_fwd that ran out of polls since the
+ * library was loaded (0 in a healthy run).  Synchronous read of a device
+ * counter. */
+FO_API int fo_ce_p2p_timeouts(unsigned int* count);
+
+/*
+ * Peer-memory plumbing (no reference counterpart).  fo_peer_export gives the
+ * CUDA IPC handle (fo_peer_handle_bytes() bytes) of the allocation holding the
+ * device pointer ptr, and ptr's offset inside it; fo_peer_open maps such a
+ * handle from another process into the current device (plain IPC mapping with
+ * peer access, no multicast) and returns the pointer at the offset;
+ * fo_peer_close unmaps it.  fo_peer_can_access reports whether device can
+ * load and store peer_device's memory.
+ */
+FO_API int fo_peer_handle_bytes(void);
+FO_API int fo_peer_export(const void* ptr, void* handle_out, int64_t* offset_out);
+FO_API int fo_peer_open(const void* handle, int64_t offset, void** ptr_out);
+FO_API int fo_peer_close(void* ptr, int64_t offset);
+FO_API int fo_peer_can_access(int device, int peer_device, int* ok);
 
 /*
  * Row-sharded cross-entropy: each rank holds a block of rows [B_local, V] of
