@@ -473,7 +473,8 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
         Bd, Hd, Ld, Dd = dins[0].shape
         toks = Bd * Ld / t
         nbytes, flops = delta_bytes(), delta_flops()
-        e = hbm_entry("chunk_gated_delta_rule", nbytes, ms, K, 1, hbm, src, traffic)
+        # three kernels per call: chunk inverses, chunk scan, range-guard recompute
+        e = hbm_entry("chunk_gated_delta_rule", nbytes, ms, K, 3, hbm, src, traffic)
         e.update({"metric": "chunk_gated_delta_rule tokens/s", "value": round(toks, 1),
                   "unit": "tokens/s (B*L per second)",
                   "tensor": {"achieved_tflops": round(flops / t / 1e12, 2), "peak_tflops": tfl,
@@ -492,6 +493,45 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
                                  "sample": f"all {Bd}x{Hd} heads, L={Ls} prefix, scaled "
                                            f"linearly to L={Ld}"}
         res["chunk_gated_delta_rule"] = e
+        del dins
+
+    if want("chunk_gated_delta_rule_d64"):
+        # head dimension 64 (the reference's own test matrix uses D <= 64): the
+        # same tensor-core kernels with channels 64..127 zero-filled by TMA
+        D64 = 64
+        ins = delta_inputs(D=D64)
+        dins = [t.to(dev) for t in ins]
+        ms = time_steps(lambda: chunk_gated_delta_rule(*dins, output_final_state=True), K, W, flush,
+                        dist)
+        t = ms / K / 1e3
+        Bd, Hd, Ld, Dd = dins[0].shape
+        nbytes, flops = delta_bytes(D=D64), delta_flops(D=D64)
+        e = hbm_entry("chunk_gated_delta_rule_d64", nbytes, ms, K, 3, hbm, src, traffic)
+        e.update({"metric": "chunk_gated_delta_rule (D=64) tokens/s",
+                  "value": round(Bd * Ld / t, 1), "unit": "tokens/s (B*L per second)",
+                  "tensor": {"achieved_tflops": round(flops / t / 1e12, 2), "peak_tflops": tfl,
+                             "frac": round(flops / t / 1e12 / tfl, 4), "algorithmic_flops": flops}})
+        # the per-step CUDA-core kernel on the same inputs (the path D < 128 took
+        # before), one call
+        import ctypes
+        from operators import _lib
+        o2 = torch.empty_like(dins[0])
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        _lib.call("fo_gdr_fwd_stepwise", *[_lib.ptr(x) for x in dins], None, _lib.ptr(o2), None,
+                  Bd, Hd, Ld, Dd, _lib.dtype_code(dins[0].dtype), _lib.dtype_code(dins[3].dtype),
+                  _lib.stream_of(dins[0]))
+        s1.record()
+        torch.cuda.synchronize(dev)
+        e["stepwise_kernel_ms"] = round(s0.elapsed_time(s1), 3)
+        # parity: head 0 against the oracle's fp32 recurrence at the full length
+        o, hT = chunk_gated_delta_rule(*dins, output_final_state=True)
+        ro, rh = oracle.delta_rule_forward(*[x[:1, :1] for x in ins], output_final_state=True)
+        ok1, d1 = _delta_close(o[:1, :1], ro)
+        ok2, d2 = _delta_close(hT[:1, :1], rh)
+        e["parity"] = "ok" if (ok1 and ok2) else f"FAIL head 0: o {d1}; state {d2}"
+        res["chunk_gated_delta_rule_d64"] = e
+        del dins, o2
     return res
 
 

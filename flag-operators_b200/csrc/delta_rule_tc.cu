@@ -168,7 +168,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
               T* __restrict__ o, float* __restrict__ hT, int* __restrict__ flags,
               const __half* __restrict__ tin, const __grid_constant__ CUtensorMap tmq,
               const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-              int64_t L) {
+              int64_t L, int D) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~(uintptr_t)1023);
@@ -189,10 +189,10 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   const int quad = warp & 3;                      // TMEM lane quadrant
   const int row = 32 * quad + lane;               // TMEM lane = accumulator row
   const int64_t head = blockIdx.x;
-  const T* qh = q + head * L * kD;
-  const T* kh = k + head * L * kD;
-  const T* vh = v + head * L * kD;
-  T* oh = o + head * L * kD;
+  // a head dimension D < 128 runs as D = 128 with zero channels: the tensor
+  // maps fill the columns past D with zeros, which leave every product, the
+  // outputs' first D channels and the state's D x D block exact
+  T* oh = o + head * L * D;
   const G* bh = beta + head * L;
   const G* gh = g + head * L;
   constexpr bool BF = false;  // operands are fp16
@@ -469,13 +469,14 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
     const int i = row;  // state row / value channel
     bool state_nz = false;
     if (h0) {
-      const float* hh = h0 + head * kD * kD;
+      const float* hh = h0 + head * D * D;
 #pragma unroll
       for (int hq = 0; hq < 4; ++hq) {
         const int j0 = 32 * hq;
         uint32_t r[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(hh[i * kD + j0 + j]);
+        for (int j = 0; j < 32; ++j)
+          r[j] = (i < D && j0 + j < D) ? __float_as_uint(hh[i * D + j0 + j]) : 0u;
         tc::tmem_st32(tm_lane + TM_S + j0, r);
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
@@ -639,9 +640,10 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       }
       tc::fence_proxy_async();
       gsync();
-      for (int e = gt_id; e < nvalid * 16; e += 128) {
-        const int t = e >> 4, ch = e & 15;
-        st_global_v4(oh + (tok0 + t) * kD + ch * 8,
+      const int nch = D >> 3;  // 16-byte chunks of an output row
+      for (int e = gt_id; e < nvalid * nch; e += 128) {
+        const int t = e / nch, ch = e - t * nch;
+        st_global_v4(oh + (tok0 + t) * D + ch * 8,
                      *reinterpret_cast<const uint4*>(sm + OFF_UT + t * 256 + ch * 16));
       }
       gsync();  // staging read before the next chunk's U^T overwrites it
@@ -651,7 +653,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
     }
     // ---- final state
     if (hT && !*s_abort) {
-      float* hh = hT + head * kD * kD;
+      float* hh = hT + head * D * D;
 #pragma unroll
       for (int hq = 0; hq < 4; ++hq) {
         uint32_t r[32];
@@ -666,8 +668,9 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         for (int j = 0; j < 32; ++j) nf = fmaf(0.f, __uint_as_float(r[j]), nf);
 #pragma unroll
         for (int j4 = 0; j4 < 8; ++j4)
-          *reinterpret_cast<uint4*>(hh + i * kD + 32 * hq + 4 * j4) =
-              make_uint4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
+          if (i < D && 32 * hq + 4 * j4 < D)
+            *reinterpret_cast<uint4*>(hh + i * D + 32 * hq + 4 * j4) =
+                make_uint4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
       }
     }
   }
@@ -708,7 +711,7 @@ constexpr uint32_t kTiCols = 64;
 template <typename T, typename G>
 __global__ void __launch_bounds__(kTiThr, 3)
 gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __restrict__ g,
-                __half* __restrict__ tout, int64_t L, int64_t items) {
+                __half* __restrict__ tout, int64_t L, int64_t items, int D) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~(uintptr_t)1023);
@@ -746,11 +749,13 @@ gdr_tinv_kernel(const T* __restrict__ k, const G* __restrict__ beta, const G* __
     const int64_t head = it / nchunks, c = it % nchunks;
     const int64_t t0 = c * kC;
     const int nvalid = (int)((L - t0) < kC ? (L - t0) : kC);
-    const T* kr = k + (head * L + t0) * kD;
+    const T* kr = k + (head * L + t0) * D;
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
+      // channels past D (D < 128) are zeros
       const int idx = p + 128 * u, t = idx >> 4, ch = idx & 15;
-      val[u] = t < nvalid ? ld_global_stream_v4(kr + t * kD + ch * 8) : make_uint4(0, 0, 0, 0);
+      val[u] = (t < nvalid && ch * 8 < D) ? ld_global_stream_v4(kr + t * D + ch * 8)
+                                           : make_uint4(0, 0, 0, 0);
     }
     if (p < 64) {
       bt = p < nvalid ? to_f<G>(beta[head * L + t0 + p]) : 0.f;
@@ -960,7 +965,7 @@ PFN_cuTensorMapEncodeTiled tensor_map_encoder() {
 template <typename T, typename G>
 int launch_tc(const void* q, const void* k, const void* v, const void* beta, const void* g,
               const float* h0, void* o, float* hT, int* flags, __half* tbuf, int64_t BH,
-              int64_t L, cudaStream_t st) {
+              int64_t L, int D, cudaStream_t st) {
   // 1. T = (I + A)^-1 of every (head, chunk), all chunks in parallel
   auto tkern = gdr_tinv_kernel<T, G>;
   // several CTAs per SM hide each other's latency: ask for the largest shared
@@ -978,13 +983,15 @@ int launch_tc(const void* q, const void* k, const void* v, const void* beta, con
   int64_t tgrid = (int64_t)num_sms() * 3;
   if (tgrid > items) tgrid = items;
   tkern<<<(unsigned)tgrid, kTiThr, kTiSmem, st>>>((const T*)k, (const G*)beta, (const G*)g, tbuf,
-                                                  L, items);
+                                                  L, items, D);
   if (int rc = check_launch("gdr_tinv_kernel")) return rc;
   // 2. the chunk scan; q, k, v reach it through TMA tensor maps
   CUtensorMap maps[3];
   const void* srcs[3] = {q, k, v};
-  const cuuint64_t gdim[3] = {(cuuint64_t)kD, (cuuint64_t)L, (cuuint64_t)BH};
-  const cuuint64_t gstride[2] = {(cuuint64_t)kD * sizeof(T), (cuuint64_t)L * kD * sizeof(T)};
+  // extent D in the channel dimension: for D < 128 the boxes past it (the
+  // second 64-channel half, and channels D..63 of the first) are zero-filled
+  const cuuint64_t gdim[3] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)BH};
+  const cuuint64_t gstride[2] = {(cuuint64_t)D * sizeof(T), (cuuint64_t)L * D * sizeof(T)};
   const cuuint32_t box[3] = {64, (cuuint32_t)kC, 1};
   const cuuint32_t estride[3] = {1, 1, 1};
   PFN_cuTensorMapEncodeTiled encode = tensor_map_encoder();
@@ -1012,19 +1019,21 @@ int launch_tc(const void* q, const void* k, const void* v, const void* beta, con
   }
   kern<<<(unsigned)BH, kThr, kSmemBytes, st>>>((const T*)q, (const T*)k, (const T*)v,
                                                (const G*)beta, (const G*)g, h0, (T*)o, hT, flags,
-                                               tbuf, maps[0], maps[1], maps[2], L);
+                                               tbuf, maps[0], maps[1], maps[2], L, D);
   return check_launch("gdr_tc_kernel");
 }
 
 template <typename T>
 int tc_gate_dispatch(int gate_dtype, const void* q, const void* k, const void* v, const void* beta,
                      const void* g, const float* h0, void* o, float* hT, int* flags,
-                     __half* tbuf, int64_t BH, int64_t L, cudaStream_t st) {
+                     __half* tbuf, int64_t BH, int64_t L, int D, cudaStream_t st) {
   switch (gate_dtype) {
-    case FO_F32: return launch_tc<T, float>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, st);
-    case FO_F16: return launch_tc<T, __half>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, st);
+    case FO_F32:
+      return launch_tc<T, float>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, D, st);
+    case FO_F16:
+      return launch_tc<T, __half>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, D, st);
     case FO_BF16:
-      return launch_tc<T, __nv_bfloat16>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, st);
+      return launch_tc<T, __nv_bfloat16>(q, k, v, beta, g, h0, o, hT, flags, tbuf, BH, L, D, st);
   }
   set_error("chunk_gated_delta_rule: unsupported gate dtype code %d", gate_dtype);
   return FO_EDTYPE;
@@ -1122,7 +1131,8 @@ inline int64_t gdr_flags_bytes(int64_t heads) { return (heads * (int64_t)sizeof(
 
 inline bool gdr_tc_eligible(const void* q, const void* k, const void* v, const void* o,
                             const float* hT, int64_t D, int dtype) {
-  return D == 128 && (dtype == FO_BF16 || dtype == FO_F16) && aligned16(q) && aligned16(k) &&
+  return (D == 16 || D == 32 || D == 64 || D == 128) && (dtype == FO_BF16 || dtype == FO_F16) &&
+         aligned16(q) && aligned16(k) &&
          aligned16(v) && aligned16(o) && (!hT || aligned16(hT));
 }
 }  // namespace
@@ -1133,7 +1143,7 @@ extern "C" int fo_gdr_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t D
   FO_CHECK_ARG(bytes && B >= 0 && H >= 0 && L >= 0, "fo_gdr_workspace_bytes: bad argument");
   // the tensor-core path: one int flag per head (fp16 range guard), then the
   // fp16 T tile of every (head, chunk) (8 KB each, 256-byte aligned)
-  if (D == 128 && (dtype == FO_BF16 || dtype == FO_F16)) {
+  if ((D == 16 || D == 32 || D == 64 || D == 128) && (dtype == FO_BF16 || dtype == FO_F16)) {
     const int64_t nc = (L + kC - 1) / kC;
     *bytes = gdr_flags_bytes(B * H) + B * H * nc * 8192;
   } else {
@@ -1175,10 +1185,11 @@ extern "C" int fo_gdr_fwd(const void* q, const void* k, const void* v, const voi
     int* flags = reinterpret_cast<int*>(workspace);
     __half* tbuf = reinterpret_cast<__half*>(reinterpret_cast<char*>(workspace) +
                                              gdr_flags_bytes(B * H));
-    int rc = dtype == FO_BF16 ? tc_gate_dispatch<__nv_bfloat16>(gate_dtype, q, k, v, beta, g, h0,
-                                                                o, hT, flags, tbuf, B * H, L, st)
-                              : tc_gate_dispatch<__half>(gate_dtype, q, k, v, beta, g, h0, o, hT,
-                                                         flags, tbuf, B * H, L, st);
+    int rc = dtype == FO_BF16
+                 ? tc_gate_dispatch<__nv_bfloat16>(gate_dtype, q, k, v, beta, g, h0, o, hT, flags,
+                                                   tbuf, B * H, L, (int)D, st)
+                 : tc_gate_dispatch<__half>(gate_dtype, q, k, v, beta, g, h0, o, hT, flags, tbuf,
+                                            B * H, L, (int)D, st);
     if (rc) return rc;
     // heads whose fp16 operands left the fp16 range: exact fp32 per-step recomputation
     // (every other head's CTA returns at once)

@@ -9,12 +9,12 @@ Keyword-only extensions (defaults keep the reference behaviour):
   initial_state=None   fp32 [B, H, D, D] state before the first token
   output_final_state=False   also return the fp32 final state: (o, h_T)
 
-Kernels: D = 128 with bf16/fp16 inputs runs the chunked tensor-core kernel
+Kernels: bf16/fp16 inputs run the chunked tensor-core kernels for every D
 (csrc/delta_rule_tc.cu: chunks of 64 tokens, seven tcgen05 GEMMs per chunk,
-fp32 state in TMEM, fp16 operand tiles); a head whose fp16 operands would leave
-the fp16 range is recomputed in the same call by the fp32 per-step kernel, so
-finite inputs give finite outputs.  Other shapes run the per-step kernel
-(csrc/delta_rule_step.cu).  _ref_forward is kept importable, as the reference's
+fp32 state in TMEM, fp16 operand tiles; D < 128 as D = 128 with zero channels);
+a head whose fp16 operands would leave the fp16 range is recomputed in the same
+call by the fp32 per-step kernel, so finite inputs give finite outputs.  fp32
+inputs run the per-step kernel (csrc/delta_rule_step.cu).  _ref_forward is kept importable, as the reference's
 tests import it; it is the reference's sequential fp32 loop on CPU tensors.
 """
 from __future__ import annotations

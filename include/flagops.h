@@ -331,7 +331,8 @@ FO_API int fo_ce_rows_fwd(const void* logits, const int64_t* target, float* loss
  * q, k, v, o: [B, H, L, D] contiguous (dtype); beta, g: [B, H, L] (gate_dtype);
  * h0: [B, H, D, D] fp32 initial state or NULL (zeros); hT: [B, H, D, D] fp32
  * final state or NULL (h0 and hT must not alias).  D in {16, 32, 64, 128}.
- * D = 128 with bf16/fp16 runs the chunked tcgen05 kernel, whose operands are
+ * bf16/fp16 inputs run the chunked tcgen05 kernel (D < 128 as D = 128 with
+ * zero channels), whose operands are
  * fp16 tiles: a head whose fp16 operands would leave the fp16 range (|x| >=
  * 65504, e.g. bf16 inputs of 1e5) is marked in the workspace (one int per head,
  * fo_gdr_workspace_bytes) and recomputed by the fp32 per-step kernel in the

@@ -205,6 +205,32 @@ def test_fp16_range_guard_flags_only_the_overflowing_head():
     _close(hT, ref_h)
 
 
+@pytest.mark.parametrize("D", [16, 32, 64])
+@pytest.mark.parametrize("L", [1, 63, 64, 65, 200, 512])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensor_core_path_small_head_dims(D, L, dtype):
+    """D < 128 runs the tensor-core kernels with channels D..127 zero-filled by
+    the tensor maps: outputs and the D x D state against the oracle, from a
+    nonzero initial state."""
+    ins = _make(2, 3, L, D, dtype, seed=7 * D + L)
+    h0 = torch.randn(2, 3, D, D, generator=torch.Generator().manual_seed(L)) * 0.1
+    o, hT = _run(ins, initial_state=h0.to(DEV), output_final_state=True)
+    ref_o, ref_h = oracle.delta_rule_forward(*ins, initial_state=h0, output_final_state=True)
+    assert o.shape == (2, 3, L, D) and hT.shape == (2, 3, D, D)
+    _close(o, ref_o)
+    _close(hT, ref_h)
+
+
+def test_small_head_dims_launch_the_tensor_core_kernels():
+    from torch.profiler import ProfilerActivity, profile
+    ins = [t.to(DEV) for t in _make(1, 2, 256, 64, seed=3)]
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        chunk_gated_delta_rule(*ins)
+        torch.cuda.synchronize()
+    names = " ".join(e.name for e in prof.events())
+    assert "gdr_tinv_kernel" in names and "gdr_tc_kernel" in names, names[:400]
+
+
 @pytest.mark.parametrize("D", [16, 32, 64, 128])
 @pytest.mark.parametrize("L", [8, 64, 256])
 def test_stepwise_path_fp32(D, L):
