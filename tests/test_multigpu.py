@@ -38,10 +38,12 @@ def _close(got, ref, dtype):
 
 def _cases():
     # (B, V, dtype, split) — split None: equal blocks; else the first block's width
-    # (the 1500-row case outgrows the peer regions' first 1024 rows)
+    # (the 1500-row case outgrows the peer regions' first 1024 rows; the 80000-
+    # column case has rows past 64 KiB per rank, which the NVLink path runs with
+    # a CTA per row instead of a warp)
     return [(64, 4096, torch.float32, None), (33, 5000, torch.float32, 1234),
             (256, 32000, torch.bfloat16, None), (17, 999, torch.float16, 500),
-            (1500, 2048, torch.float32, None)]
+            (1500, 2048, torch.float32, None), (40, 80000, torch.float32, None)]
 
 
 def _worker(rank, port, q):
