@@ -138,6 +138,25 @@ __device__ __forceinline__ uint4 scale8h(uint4 u, __half2 s) {
   return u;
 }
 
+// 8 input elements times a scale, as fp16 operand elements: fp16 input in
+// half2 arithmetic (as above); bf16 input unpacked, scaled in fp32 and rounded
+// once to fp16
+template <typename T>
+__device__ __forceinline__ uint4 scale8_op(uint4 u, float s) {
+  if constexpr (std::is_same<T, __half>::value) {
+    return scale8h(u, __float2half2_rn(s));
+  } else {
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(__uint_as_float(w[i] << 16) * s,
+                                          __uint_as_float(w[i] & 0xffff0000u) * s);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return u;
+  }
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -195,7 +214,8 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
   T* oh = o + head * L * D;
   const G* bh = beta + head * L;
   const G* gh = g + head * L;
-  constexpr bool BF = false;  // operands are fp16
+  constexpr bool BF = false;  // operands are fp16 (except MMA (a): the input type)
+  constexpr bool kInBF = std::is_same<T, __nv_bfloat16>::value;
   const int64_t nchunks = (L + kC - 1) / kC;
   const int bar_id = is_chain ? 1 : 2;            // named barrier of the group
 
@@ -345,19 +365,17 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         sNeg[p] += sNeg[31];
       }
       if constexpr (!std::is_same<T, __half>::value) {
-        // bf16 -> fp16 in place over the set's 48 KB (the swizzle does not
-        // matter elementwise): 24 chunks of 16 bytes per thread, 8 in flight
+        // bf16 -> fp16 in place over the V tile (16 KB; the swizzle does not
+        // matter elementwise): 8 chunks of 16 bytes per thread, all in flight.
+        // Q and K stay bf16: MMA (a) takes them as they landed, and the scaled
+        // copies convert while they scale.
+        uint4 val[8];
 #pragma unroll
-        for (int u0 = 0; u0 < 24; u0 += 8) {
-          uint4 val[8];
+        for (int u = 0; u < 8; ++u)
+          val[u] = *reinterpret_cast<const uint4*>(sm + Vs + (uint32_t)(p + 128 * u) * 16);
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            val[u] = *reinterpret_cast<const uint4*>(sm + QKs + (uint32_t)(p + 128 * (u0 + u)) * 16);
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            *reinterpret_cast<uint4*>(sm + QKs + (uint32_t)(p + 128 * (u0 + u)) * 16) =
-                to_op8<T>(val[u]);
-        }
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(sm + Vs + (uint32_t)(p + 128 * u) * 16) = to_op8<T>(val[u]);
       }
       tc::fence_proxy_async();
       gsync();
@@ -372,9 +390,9 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
         sKts[p] = gt.ratio(kC - 1, p) * sBeta[p];
         if (p == 0) *reinterpret_cast<float*>(G0 + G_GC) = gt.ratio(kC - 1, -1);
       }
-      // ---- (a) [Q;K] K^T -> QK[b]
+      // ---- (a) [Q;K] K^T -> QK[b], on the input tiles (bf16 x bf16 or fp16 x fp16)
       if (p == 0) {
-        constexpr uint32_t id_a = tc::idesc_f16(128, 64, BF, false, false);
+        constexpr uint32_t id_a = tc::idesc_f16(128, 64, kInBF, false, false);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t h = ks >> 2, kk = ks & 3;
@@ -411,12 +429,12 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
             const int half = ch >> 3, cc = ch & 7;
             if (m == 0) {
               *reinterpret_cast<uint4*>(sm + OFF_GQ + half * 8192 + tc::sw128_chunk(t, cc)) =
-                  scale8h(raw[u], __float2half2_rn(sGam[t]));
+                  scale8_op<T>(raw[u], sGam[t]);
             } else {
               *reinterpret_cast<uint4*>(sm + OFF_KT + half * 8192 + tc::sw128_chunk(t, cc)) =
-                  scale8h(raw[u], __float2half2_rn(sKts[t]));
+                  scale8_op<T>(raw[u], sKts[t]);
               *reinterpret_cast<uint4*>(sm + QKs + half * 16384 + tc::sw128_chunk(64 + t, cc)) =
-                  scale8h(raw[u], __float2half2_rn(sGamP[t]));
+                  scale8_op<T>(raw[u], sGamP[t]);
             }
           }
         }
@@ -493,6 +511,10 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       tc::fence_proxy_async();
       state_nz = true;
     }
+    // The state in TMEM enters chunk c already multiplied by gamma_{C-1} of
+    // chunk c (the previous chunk's state copy applies it), so (g) accumulates
+    // onto it directly; (d),(e) read the undecayed fp16 copy.
+    bool prep_ready = false;  // bar_prep of this chunk already waited for
     for (int64_t c = 0; c < nchunks; ++c) {
       const int b = (int)(c & 1);
       const uint32_t ph = (uint32_t)(c & 1);
@@ -503,7 +525,8 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       const int* sZ = reinterpret_cast<const int*>(G0 + G_Z);
       const int* sNeg = reinterpret_cast<const int*>(G0 + G_NEG);
       const float* sSB = reinterpret_cast<const float*>(G0 + G_SB);
-      if (gwait(bar_prep, ph)) break;
+      if (!prep_ready && gwait(bar_prep, ph)) break;
+      prep_ready = false;
       // ---- (d) U^T[b] += S (-W)^T,  (e) O^T = S (gQ)^T   (need the state)
       if (gt_id == 0) {
         if (state_nz) {
@@ -571,7 +594,8 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
           *reinterpret_cast<uint4*>(sm + OFF_UT + tc::sw128_chunk(i, 4 * hf + c4)) = pk;
         }
       }
-      if (state_nz) {
+      if (state_nz && c == 0) {
+        // the initial state: decayed here (later chunks' by the state copy)
         const float gc = *reinterpret_cast<const float*>(G0 + G_GC);
 #pragma unroll
         for (int hq = 0; hq < 4; ++hq) {
@@ -607,7 +631,7 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
       }
       if (gwait(bar_b2, ph)) break;
       state_nz = true;
-      // ---- O^T -> staging [t][i] (U^T buffer, consumed), state -> fp16 operand copy
+      // ---- O^T -> staging [t][i] (U^T buffer, consumed) -> global
       {
         uint32_t r[32];
         T* so = reinterpret_cast<T*>(sm + OFF_UT);
@@ -622,6 +646,27 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
             so[(32 * hf + j) * kD + i] = from_f<T>(x);
           }
         }
+      }
+      gsync();
+      const int nch = D >> 3;  // 16-byte chunks of an output row
+      for (int e = gt_id; e < nvalid * nch; e += 128) {
+        const int t = e / nch, ch = e - t * nch;
+        st_global_v4(oh + (tok0 + t) * D + ch * 8,
+                     *reinterpret_cast<const uint4*>(sm + OFF_UT + t * 256 + ch * 16));
+      }
+      gsync();  // staging read before the next chunk's U^T overwrites it
+      if (gt_id == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar_done + b))
+                     : "memory");
+      // ---- the state for chunk c + 1: its fp16 operand copy (undecayed, for
+      // (d),(e)), and the TMEM state multiplied by chunk c + 1's gamma_{C-1}
+      // (what (g) accumulates onto), in one pass over the state
+      if (c + 1 < nchunks) {
+        if (gwait(bar_prep, ph ^ 1u)) break;  // chunk c + 1's gate table is ready
+        prep_ready = true;
+        const float gn = *reinterpret_cast<const float*>(gtab(b ^ 1) + G_GC);
+        const float2 g2 = make_float2(gn, gn);
+        uint32_t r[32];
 #pragma unroll
         for (int hq = 0; hq < 4; ++hq) {
           tc::tmem_ld32(tm_lane + TM_S + 32 * hq, r);
@@ -636,20 +681,18 @@ gdr_tc_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restr
             *reinterpret_cast<uint4*>(sm + OFF_S + (hq >> 1) * 16384 +
                                       tc::sw128_chunk(i, 4 * (hq & 1) + c4)) = pk;
           }
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float2 m2 = mul2(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), g2);
+            r[j] = __float_as_uint(m2.x);
+            r[j + 1] = __float_as_uint(m2.y);
+          }
+          tc::tmem_st32(tm_lane + TM_S + 32 * hq, r);
         }
+        tc::tmem_wait_st();
+        tc::fence_proxy_async();
+        gsync();
       }
-      tc::fence_proxy_async();
-      gsync();
-      const int nch = D >> 3;  // 16-byte chunks of an output row
-      for (int e = gt_id; e < nvalid * nch; e += 128) {
-        const int t = e / nch, ch = e - t * nch;
-        st_global_v4(oh + (tok0 + t) * D + ch * 8,
-                     *reinterpret_cast<const uint4*>(sm + OFF_UT + t * 256 + ch * 16));
-      }
-      gsync();  // staging read before the next chunk's U^T overwrites it
-      if (gt_id == 0)
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar_done + b))
-                     : "memory");
     }
     // ---- final state
     if (hT && !*s_abort) {
