@@ -1386,8 +1386,9 @@ median_cta_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __rest
 // ---------------------------------------------------------------------------
 // Every CTA owns a contiguous chunk of x.  Per pass, each CTA histograms the
 // digit of its chunk's elements that match the prefix selected so far into
-// shared memory and adds its non-empty bins to a global histogram; one CTA
-// then picks the bin holding rank r and clears the histogram.  After the last
+// shared memory and adds its non-empty bins to a global histogram; the last CTA
+// of the pass to finish (threadfence + ticket) then picks the bin holding rank
+// r and clears the histogram, so a pass is one launch.  After the last
 // pass the key is known and gives the value, except for the key that +0.0 and
 // -0.0 share: then each CTA counts its zeros and one CTA walks the chunk holding
 // the r-th zero in index order and returns it, sign included.  The first NaN
@@ -1395,13 +1396,14 @@ median_cta_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __rest
 constexpr int kGmThreads = 512;
 constexpr int kGmBins = 2048;
 constexpr int kGmMaxCtas = 1024;
-static_assert(kGmMaxCtas <= 2 * kGmThreads, "gm_pick_kernel scans two counts per thread");
+static_assert(kGmMaxCtas <= 2 * kGmThreads, "gm_pick_block scans two counts per thread");
 constexpr int64_t kGmMinN = (int64_t)1 << 20;
 
 struct GmState {
   unsigned long long prefix, mask, r, first_nan;
   unsigned long long bin_cnt;  // elements in the bin selected by the last pass
   unsigned int ovf;            // 1: the candidates of pass 1 were not (all) kept
+  unsigned int ticket;         // CTAs of the current kernel that finished (last one finishes up)
 };
 
 // Geometry of the grid path: G CTAs with chunks of a multiple of 2048 elements
@@ -1476,8 +1478,93 @@ __global__ void gm_init_kernel(GmState* s, uint32_t* hist, int64_t k) {
     s->first_nan = ~0ull;
     s->bin_cnt = 0;
     s->ovf = 0;
+    s->ticket = 0;
   }
   for (int j = threadIdx.x; j < kGmBins; j += blockDim.x) hist[j] = 0;
+}
+
+// True in exactly one CTA of the grid: the last to get here, after every CTA's
+// global writes before this point are visible to it (threadfence + ticket).
+// The ticket is reset for the next kernel.
+__device__ __forceinline__ bool gm_last_cta(GmState* s) {
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_last = atomicAdd(&s->ticket, 1u) == gridDim.x - 1;
+    if (s_last) s->ticket = 0;
+  }
+  __syncthreads();
+  if (s_last) __threadfence();
+  return s_last != 0;
+}
+
+// The bin holding rank r (kGmThreads threads, 4 bins each), run by the last CTA
+// of a histogram pass; clears the histogram for the next pass.
+template <typename T>
+__device__ __forceinline__ void gm_find_block(GmState* s, uint32_t* hist, int p,
+                                              const T* __restrict__ x, T* __restrict__ value) {
+  using K = typename KeyTraits<T>::K;
+  using D = Digits<K>;
+  static_assert(kGmBins == 4 * kGmThreads, "4 bins per thread");
+  __shared__ uint32_t fsum[kGmThreads / 32];
+  __shared__ uint32_t f_bin, f_below, f_cnt;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  uint32_t c[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = __ldcg(hist + 4 * tid + i);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hist[4 * tid + i] = 0;
+  const unsigned long long fnan = *(volatile unsigned long long*)&s->first_nan;
+  if (fnan != ~0ull) {
+    // a NaN decides (pass 0 looked at every element): its value, as stored
+    if (tid == 0 && p == 0) *value = x[fnan];
+    return;
+  }
+  const uint32_t tot = c[0] + c[1] + c[2] + c[3];
+  uint32_t inc = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) fsum[wid] = inc;
+  __syncthreads();
+  uint32_t off = 0;
+  for (int q = 0; q < wid; ++q) off += fsum[q];
+  const uint64_t exc = (uint64_t)off + inc - tot;
+  const uint64_t r = *(volatile unsigned long long*)&s->r;
+  if (exc <= r && r < exc + tot) {
+    uint64_t acc = exc;
+    int w = 0;
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+      if (w == i && r >= acc + c[i]) {
+        acc += c[i];
+        w = i + 1;
+      }
+    uint32_t cw = c[0];
+#pragma unroll
+    for (int i = 1; i < 4; ++i)
+      if (w == i) cw = c[i];
+    f_bin = 4 * tid + w;
+    f_below = (uint32_t)acc;
+    f_cnt = cw;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const int sh = D::shift(p);
+    const uint32_t dmask = (1u << D::width(p)) - 1u;
+    s->r = r - f_below;
+    s->bin_cnt = f_cnt;
+    s->prefix |= (unsigned long long)((K)f_bin << sh);
+    s->mask |= (unsigned long long)((K)dmask << sh);
+    // after the last pass the key is known: it gives the value unless it is
+    // the key +0.0 and -0.0 share (then gm_count_kernel picks the element)
+    const K key = (K)s->prefix;
+    if (p == D::kPasses - 1 && !KeyTraits<T>::is_zero_key(key)) *value = KeyTraits<T>::from_key(key);
+    __threadfence();
+  }
 }
 
 // MODE 0: the first pass (every element counts; NaNs are looked for).
@@ -1489,13 +1576,15 @@ template <typename T, int MODE>
 __global__ void __launch_bounds__(kGmThreads)
 gm_hist_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
                uint32_t* __restrict__ hist, int p, typename KeyTraits<T>::K* __restrict__ cand,
-               uint32_t* __restrict__ ncand, int64_t R, int64_t G) {
+               uint32_t* __restrict__ ncand, int64_t R, int64_t G, T* __restrict__ value) {
   using Tr = KeyTraits<T>;
   using K = typename Tr::K;
   using D = Digits<K>;
   __shared__ uint32_t h[kGmBins];
   __shared__ uint32_t s_nc;
-  if (MODE > 0 && *(volatile unsigned long long*)&s->first_nan != ~0ull) return;  // NaN decided
+  // a NaN found by pass 0 decides: every CTA of a later pass returns at once
+  // (all of them, so no ticket is taken and none is left over)
+  if (MODE > 0 && *(volatile unsigned long long*)&s->first_nan != ~0ull) return;
   const K prefix = (K)s->prefix, mask = (K)s->mask;
   const int sh = D::shift(p);
   const uint32_t nb = 1u << D::width(p), dmask = nb - 1u;
@@ -1550,86 +1639,16 @@ gm_hist_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
   __syncthreads();
   for (uint32_t j = threadIdx.x; j < nb; j += kGmThreads)
     if (h[j]) atomicAdd(hist + j, h[j]);
-}
-
-// One CTA of 1024 threads (2 bins each): the bin holding rank r.
-template <typename T>
-__global__ void __launch_bounds__(1024) gm_find_kernel(GmState* s, uint32_t* hist, int p) {
-  using K = typename KeyTraits<T>::K;
-  using D = Digits<K>;
-  __shared__ uint32_t wsum[32];
-  __shared__ uint32_t s_bin, s_below, s_cnt;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const uint32_t c0 = hist[2 * tid], c1 = hist[2 * tid + 1];
-  __syncthreads();
-  hist[2 * tid] = 0;
-  hist[2 * tid + 1] = 0;
-  if (s->first_nan != ~0ull) return;
-  const uint32_t tot = c0 + c1;
-  uint32_t inc = tot;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += y;
-  }
-  if (lane == 31) wsum[wid] = inc;
-  __syncthreads();
-  uint32_t off = 0;
-  for (int q = 0; q < wid; ++q) off += wsum[q];
-  const uint64_t exc = (uint64_t)off + inc - tot;
-  const uint64_t r = s->r;
-  if (exc <= r && r < exc + tot) {
-    if (r < exc + c0) {
-      s_bin = 2 * tid;
-      s_below = (uint32_t)exc;
-      s_cnt = c0;
-    } else {
-      s_bin = 2 * tid + 1;
-      s_below = (uint32_t)(exc + c0);
-      s_cnt = c1;
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    const int sh = D::shift(p);
-    const uint32_t dmask = (1u << D::width(p)) - 1u;
-    s->r = r - s_below;
-    s->bin_cnt = s_cnt;
-    s->prefix |= (unsigned long long)((K)s_bin << sh);
-    s->mask |= (unsigned long long)((K)dmask << sh);
-  }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kGmThreads)
-gm_count_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, const GmState* s,
-                uint32_t* __restrict__ cnt) {
-  using Tr = KeyTraits<T>;
-  using K = typename Tr::K;
-  __shared__ uint32_t red[kGmThreads / 32];
-  if (s->first_nan != ~0ull) return;
-  const K key = (K)s->prefix;
-  if (!Tr::is_zero_key(key)) return;  // the key alone gives the value
-  const int64_t j0 = (int64_t)blockIdx.x * chunk;
-  const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
-  uint32_t c = 0;
-  gm_for_chunk<T>(x, j0, j1, [&](int64_t, T v) { c += (Tr::key(v) == key) ? 1u : 0u; });
-  c = __reduce_add_sync(0xffffffffu, c);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = c;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t t = 0;
-    for (int q = 0; q < kGmThreads / 32; ++q) t += red[q];
-    cnt[blockIdx.x] = t;
-  }
+  // the last CTA of the pass picks the bin (no separate launch)
+  if (gm_last_cta(s)) gm_find_block<T>(s, hist, p, x, value);
 }
 
 // One CTA: the chunk holding the r-th element with the selected key, then the
 // element itself in index order.
 template <typename T>
-__global__ void __launch_bounds__(kGmThreads)
-gm_pick_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, const GmState* s,
-               const uint32_t* __restrict__ cnt, int G, T* __restrict__ value) {
+__device__ __forceinline__ void gm_pick_block(const T* __restrict__ x, int64_t n, int64_t chunk,
+                                              const GmState* s, const uint32_t* __restrict__ cnt,
+                                              int G, T* __restrict__ value) {
   using Tr = KeyTraits<T>;
   using K = typename Tr::K;
   __shared__ uint32_t wsum[kGmThreads / 32];
@@ -1637,21 +1656,13 @@ gm_pick_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, const GmState*
   __shared__ unsigned long long s_r;
   __shared__ long long s_found;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  if (s->first_nan != ~0ull) {
-    if (tid == 0) *value = x[s->first_nan];
-    return;
-  }
   const K key = (K)s->prefix;
-  if (!Tr::is_zero_key(key)) {
-    if (tid == 0) *value = Tr::from_key(key);
-    return;
-  }
   // +0.0 and -0.0 share the key: the chunk holding the r-th zero, from a
   // block-wide inclusive scan of the per-CTA counts (two per thread).
   __shared__ unsigned long long wtot[kGmThreads / 32];
   const unsigned long long r0 = s->r;
-  const uint32_t a0 = (2 * tid < G) ? cnt[2 * tid] : 0u;
-  const uint32_t a1 = (2 * tid + 1 < G) ? cnt[2 * tid + 1] : 0u;
+  const uint32_t a0 = (2 * tid < G) ? __ldcg(cnt + 2 * tid) : 0u;
+  const uint32_t a1 = (2 * tid + 1 < G) ? __ldcg(cnt + 2 * tid + 1) : 0u;
   unsigned long long inc = (unsigned long long)a0 + a1;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -1700,6 +1711,35 @@ gm_pick_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, const GmState*
   if (tid == 0) *value = s_found >= 0 ? x[s_found] : x[j0];
 }
 
+
+// Only when the key is the one +0.0 and -0.0 share (the value was written
+// otherwise): each CTA counts the zeros of its chunk, and the last CTA picks the
+// r-th zero in index order (gm_pick_block).
+template <typename T>
+__global__ void __launch_bounds__(kGmThreads)
+gm_count_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
+                uint32_t* __restrict__ cnt, T* __restrict__ value) {
+  using Tr = KeyTraits<T>;
+  using K = typename Tr::K;
+  __shared__ uint32_t red[kGmThreads / 32];
+  if (s->first_nan != ~0ull) return;
+  const K key = (K)s->prefix;
+  if (!Tr::is_zero_key(key)) return;  // the key alone gave the value
+  const int64_t j0 = (int64_t)blockIdx.x * chunk;
+  const int64_t j1 = (j0 + chunk < n) ? j0 + chunk : n;
+  uint32_t c = 0;
+  gm_for_chunk<T>(x, j0, j1, [&](int64_t, T v) { c += (Tr::key(v) == key) ? 1u : 0u; });
+  c = __reduce_add_sync(0xffffffffu, c);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int q = 0; q < kGmThreads / 32; ++q) t += red[q];
+    cnt[blockIdx.x] = t;
+  }
+  if (gm_last_cta(s)) gm_pick_block<T>(x, n, chunk, s, cnt, (int)gridDim.x, value);
+}
+
 template <typename T>
 int launch_grid_median(const void* xv, void* value, int64_t n, void* ws, cudaStream_t st) {
   using K = typename KeyTraits<T>::K;
@@ -1711,21 +1751,22 @@ int launch_grid_median(const void* xv, void* value, int64_t n, void* ws, cudaStr
   K* cand = reinterpret_cast<K*>((char*)ws + kGmCandOff);
   const GmGeo geo = gm_geo(n);
   const int64_t G = geo.G, chunk = geo.chunk, R = geo.R;
+  // one launch per pass: its last CTA picks the bin (and, after the last pass,
+  // writes the value); the count kernel does work only for the +-0 key
+  T* out = (T*)value;
   gm_init_kernel<<<1, 256, 0, st>>>(s, hist, (n - 1) / 2);
   for (int p = 0; p < Digits<K>::kPasses; ++p) {
     if (p == 0)
       gm_hist_kernel<T, 0><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p, cand,
-                                                               ncand, R, G);
+                                                               ncand, R, G, out);
     else if (p == 1)
       gm_hist_kernel<T, 1><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p, cand,
-                                                               ncand, R, G);
+                                                               ncand, R, G, out);
     else
       gm_hist_kernel<T, 2><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, hist, p, cand,
-                                                               ncand, R, G);
-    gm_find_kernel<T><<<1, 1024, 0, st>>>(s, hist, p);
+                                                               ncand, R, G, out);
   }
-  gm_count_kernel<T><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, cnt);
-  gm_pick_kernel<T><<<1, kGmThreads, 0, st>>>(x, n, chunk, s, cnt, (int)G, (T*)value);
+  gm_count_kernel<T><<<(unsigned)G, kGmThreads, 0, st>>>(x, n, chunk, s, cnt, out);
   return check_launch("global median");
 }
 

@@ -150,24 +150,27 @@ rms_dw_chunk_kernel(const T* __restrict__ dy, const T* __restrict__ x,
   dw_part[(int64_t)blockIdx.y * N + j] = a;
 }
 
-// dw[j] = sum over the G partial rows.  A CTA owns 32 columns: warp q adds rows
-// q, q + 8, ... (lane = column, 128-byte coalesced rows), then warp 0 adds the
-// 8 warp sums in order, so the result does not depend on scheduling.
+// dw[j] = sum over the G partial rows.  A CTA owns 32 columns: warp q of 32
+// adds rows q, q + 32, ... (lane = column, 128-byte coalesced rows; ~5 rows per
+// warp for one CTA per SM, so each chain of dependent adds is short), then warp
+// 0 adds the 32 warp sums in order, so the result does not depend on
+// scheduling.
+constexpr int kDwWarps = 32;
 template <typename W>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32 * kDwWarps)
 rms_dw_reduce_kernel(const float* __restrict__ dw_part, int G, int64_t N, W* __restrict__ dw) {
-  __shared__ float acc[8][32];
+  __shared__ float acc[kDwWarps][33];
   const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
   const int64_t j = (int64_t)blockIdx.x * 32 + lane;
   float a = 0.f;
   if (j < N)
-    for (int g = q; g < G; g += 8) a += dw_part[(int64_t)g * N + j];
+    for (int g = q; g < G; g += kDwWarps) a += dw_part[(int64_t)g * N + j];
   acc[q][lane] = a;
   __syncthreads();
   if (q == 0 && j < N) {
     float t = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) t += acc[k][lane];
+    for (int k = 0; k < kDwWarps; ++k) t += acc[k][lane];
     dw[j] = from_f<W>(t);
   }
 }
@@ -216,7 +219,7 @@ int run_bwd(const void* dy, const void* x, const void* w, const float* inv, void
     rms_dw_chunk_kernel<T><<<gc, 256, 0, st>>>((const T*)dy, (const T*)x, inv, part, M, N);
     if (int rc = check_launch("rms_dw_chunk_kernel")) return rc;
   }
-  rms_dw_reduce_kernel<W><<<(unsigned)((N + 31) / 32), 256, 0, st>>>(part, G, N, (W*)dw);
+  rms_dw_reduce_kernel<W><<<(unsigned)((N + 31) / 32), 32 * kDwWarps, 0, st>>>(part, G, N, (W*)dw);
   return check_launch("rms_dw_reduce_kernel");
 }
 
