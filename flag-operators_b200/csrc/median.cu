@@ -1429,7 +1429,10 @@ constexpr int64_t kGmCandOff = 256 + 4 * (kGmBins + 2 * kGmMaxCtas);
 // 16-byte aligned: 16-byte loads in batches of 4 per thread, software-pipelined
 // (the next batch is in flight while the current one is processed); element
 // loads for the ragged end, and for the whole range otherwise.
-template <typename T, typename F>
+// POL: 0 default L2 policy; 1 evict_last (pass 0: x stays in L2 for pass 1);
+// 2 evict_first (pass 1: the last read of x, which also demotes the lines
+// pass 0 kept).
+template <typename T, int POL = 0, typename F>
 __device__ __forceinline__ void gm_for_chunk(const T* __restrict__ x, int64_t j0, int64_t j1, F&& f) {
   constexpr int E = 16 / (int)sizeof(T);
   constexpr int U = 4;
@@ -1438,10 +1441,13 @@ __device__ __forceinline__ void gm_for_chunk(const T* __restrict__ x, int64_t j0
   if ((reinterpret_cast<uintptr_t>(x + j0) & 15) == 0) {
     const int64_t nv = (j1 - j0) / E;
     const uint4* __restrict__ xv = reinterpret_cast<const uint4*>(x + j0);
+    const uint64_t pol = POL == 1 ? l2_policy_evict_last() : l2_policy_evict_first();
     auto load = [&](uint4* r, int64_t v) {
 #pragma unroll
       for (int u = 0; u < U; ++u)
-        if (v + u * kGmThreads < nv) r[u] = __ldg(xv + v + u * kGmThreads);
+        if (v + u * kGmThreads < nv)
+          r[u] = POL == 0 ? __ldg(xv + v + u * kGmThreads)
+                          : ld_global_hint_v4(xv + v + u * kGmThreads, pol);
     };
     auto proc = [&](const uint4* r, int64_t v) {
 #pragma unroll
@@ -1597,14 +1603,14 @@ gm_hist_kernel(const T* __restrict__ x, int64_t n, int64_t chunk, GmState* s,
   K* mine = cand + blockIdx.x * R;
   unsigned long long my_nan = ~0ull;
   if (MODE == 0) {
-    gm_for_chunk<T>(x, j0, j1, [&](int64_t j, T v) {
+    gm_for_chunk<T, 1>(x, j0, j1, [&](int64_t j, T v) {
       if (Tr::isnan_(v) && (unsigned long long)j < my_nan) my_nan = (unsigned long long)j;
       atomicAdd(h + ((uint32_t)(Tr::key(v) >> sh) & dmask), 1u);
     });
     if (my_nan != ~0ull) atomicMin(&s->first_nan, my_nan);
   } else if (MODE == 1) {
     const bool keep = s->bin_cnt <= (unsigned long long)(G * R);
-    gm_for_chunk<T>(x, j0, j1, [&](int64_t, T v) {
+    gm_for_chunk<T, 2>(x, j0, j1, [&](int64_t, T v) {
       const K kk = Tr::key(v);
       if ((kk & mask) == prefix) {
         atomicAdd(h + ((uint32_t)(kk >> sh) & dmask), 1u);
