@@ -98,6 +98,10 @@ class _FusedCrossEntropy(torch.autograd.Function):
         return dlogits, None, None, None, None
 
 
+class _PeerUnavailable(RuntimeError):
+    """Some rank of the group could not set up or map the exchange regions."""
+
+
 class _PeerRegions:
     """The NVLink exchange regions of one process group on this rank's device.
 
@@ -106,6 +110,11 @@ class _PeerRegions:
     the group and each rank maps the other ranks' regions, so the fused kernel
     stores its per-row statistics straight into every rank's region.  The
     regions grow (re-exchanged) when a call has more rows than they hold.
+
+    Every rank runs the same collectives whatever fails locally, and the
+    outcome is agreed over the group: if any rank could not allocate, export
+    or map a region, every rank unmaps what it mapped and raises
+    _PeerUnavailable, so no rank is left waiting on another.
     """
 
     def __init__(self, group, dev, rows):
@@ -113,31 +122,52 @@ class _PeerRegions:
         self.group, self.dev = group, dev
         self.P, self.rank = dist.get_world_size(group), dist.get_rank(group)
         self.cap = int(rows)
-        nbytes = ctypes.c_int64()
-        _lib.call("fo_ce_shard_p2p_region_bytes", self.P, self.cap, ctypes.byref(nbytes))
-        self.region = torch.zeros(nbytes.value, dtype=torch.uint8, device=dev)
-        torch.cuda.synchronize(dev)  # zeroed before any peer can map and write it
-        hb = _lib.load().fo_peer_handle_bytes()
-        handle = (ctypes.c_uint8 * hb)()
-        off = ctypes.c_int64()
-        _lib.call("fo_peer_export", _lib.ptr(self.region), handle, ctypes.byref(off))
-        entries = [None] * self.P
-        dist.all_gather_object(entries, (bytes(handle), off.value), group=group)
         self.ptrs, self.opened = [], []
-        for p, (h, o) in enumerate(entries):
-            if p == self.rank:
-                self.ptrs.append(self.region.data_ptr())
-                continue
-            out = ctypes.c_void_p()
-            hbuf = (ctypes.c_uint8 * hb).from_buffer_copy(h)
-            _lib.call("fo_peer_open", hbuf, o, ctypes.byref(out))
-            self.ptrs.append(out.value)
-            self.opened.append((out.value, o))
+        self.region = None
+        hb = _lib.load().fo_peer_handle_bytes()
+        err = None
+        entry = None
+        try:
+            nbytes = ctypes.c_int64()
+            _lib.call("fo_ce_shard_p2p_region_bytes", self.P, self.cap, ctypes.byref(nbytes))
+            self.region = torch.zeros(nbytes.value, dtype=torch.uint8, device=dev)
+            if dev.type == "cuda":
+                torch.cuda.synchronize(dev)  # zeroed before any peer can map and write it
+            handle = (ctypes.c_uint8 * hb)()
+            off = ctypes.c_int64()
+            _lib.call("fo_peer_export", _lib.ptr(self.region), handle, ctypes.byref(off))
+            entry = (bytes(handle), off.value)
+        except (RuntimeError, ValueError) as e:
+            err = e
+        entries = [None] * self.P
+        dist.all_gather_object(entries, entry, group=group)
+        if err is None and any(e is None for e in entries):
+            err = RuntimeError("another rank could not export its region")
+        if err is None:
+            try:
+                for p, (h, o) in enumerate(entries):
+                    if p == self.rank:
+                        self.ptrs.append(self.region.data_ptr())
+                        continue
+                    out = ctypes.c_void_p()
+                    hbuf = (ctypes.c_uint8 * hb).from_buffer_copy(h)
+                    _lib.call("fo_peer_open", hbuf, o, ctypes.byref(out))
+                    self.ptrs.append(out.value)
+                    self.opened.append((out.value, o))
+            except (RuntimeError, ValueError) as e:
+                err = e
+        oks = [None] * self.P
+        dist.all_gather_object(oks, err is None, group=group)
+        if not all(oks):
+            self.close()
+            raise _PeerUnavailable(f"NVLink exchange regions unavailable on rank {self.rank}: "
+                                   f"{err if err is not None else 'another rank failed'}")
         self.table = (ctypes.c_void_p * self.P)(*self.ptrs)
         self.epoch = 0
 
     def close(self):
-        torch.cuda.synchronize(self.dev)  # no kernel of this rank still uses the mappings
+        if self.dev.type == "cuda":
+            torch.cuda.synchronize(self.dev)  # no kernel of this rank still uses the mappings
         for ptr_, off in self.opened:
             _lib.call("fo_peer_close", ctypes.c_void_p(ptr_), off)
         self.opened = []
@@ -183,7 +213,11 @@ def _peer_regions(group, dev, rows):
         # more rows than the regions hold: every rank re-allocates at this call
         # (the new regions are zeroed, so the epochs start again at 1)
         st.close()
-    st = _PeerRegions(group, dev, max(int(rows), 1024))
+    try:
+        st = _PeerRegions(group, dev, max(int(rows), 1024))
+    except _PeerUnavailable:
+        _PEER[key] = False  # every rank got here: the all-gather path from now on
+        return None
     _PEER[key] = st
     return st
 

@@ -127,3 +127,65 @@ def test_shard_layout_rules():
     assert shard_layout(0, 2, 30, vocab_offset=0, vocab_size=50) == (0, 50)
     with pytest.raises(ValueError):
         shard_layout(3, 4, 100, vocab_size=350)
+
+
+def _peer_worker(rank, world, port, q):
+    """Rank 1 fails to map rank 0's region (a simulated fo_peer_open error);
+    rank 0 maps rank 1's.  Both must give up together and rank 0 must unmap
+    what it mapped.  The library calls that would touch GPU memory are
+    replaced by stand-ins (no pointer is ever dereferenced here)."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from operators import _lib
+        from operators import fused_cross_entropy as fce
+        real_call, closed = _lib.call, []
+
+        def fake_call(name, *args):
+            if name == "fo_peer_export":
+                args[2]._obj.value = 0  # byref(offset)
+                return None
+            if name == "fo_peer_open":
+                if rank == 1:
+                    raise RuntimeError("fo_peer_open: simulated mapping failure")
+                args[2]._obj.value = 0x1000
+                return None
+            if name == "fo_peer_close":
+                closed.append(args[1])
+                return None
+            return real_call(name, *args)
+
+        _lib.call = fake_call
+        try:
+            fce._PeerRegions(dist.group.WORLD, torch.device("cpu"), 16)
+            res = "no error"
+        except fce._PeerUnavailable as e:
+            res = ("unavailable", len(closed), str(e))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, repr(e)))
+
+
+def test_peer_regions_setup_failure_is_agreed():
+    """The NVLink cross-entropy path is set up by every rank or by none: a
+    mapping failure on one rank makes every rank fall back (no rank is left
+    waiting on a peer that will never write)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        out = dict(q.get(timeout=120) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+    assert isinstance(out[0], tuple) and out[0][0] == "unavailable", out
+    assert isinstance(out[1], tuple) and out[1][0] == "unavailable", out
+    assert out[0][1] == 1, f"rank 0 should unmap the one region it mapped: {out[0]}"
+    assert out[1][1] == 0, out
