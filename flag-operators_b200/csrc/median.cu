@@ -510,44 +510,44 @@ __device__ __forceinline__ bool ws_wait(WsSmem& S, uint64_t* bar, uint32_t parit
   return false;
 }
 
-// Bin orders of ws_find: kOrdPlain = bins ascending (digit histograms of keys);
+// Bin orders of bin_find: kOrdPlain = bins ascending (digit histograms of keys);
 // kOrdF32 / kOrdI32 = raw top-11-bit bins of float / int32 words in value order.
 constexpr int kOrdPlain = 0, kOrdF32 = 1, kOrdI32 = 2;
 
-// Consumer scan of a slot's 2048 bins.  Lane l reads the 16-byte chunks
-// 32 j + l (j = 0..15: bins 128 j + 4 l .. + 3), so every read is free of bank
-// conflicts; group j of 128 bins is visited in value order, descending inside
-// for the negative float groups.  Returns to every lane the raw bin holding rank
-// r, the count below it (in value order) and its count, and zeroes the bins.
-// With `edge` (floats), `special` reports a nonzero count in the first 4 bins of
-// the value order or more than npad in the last 4 (NaN and infinite words).
-// z0 / z1024 return the counts of raw bins 0 and 1024 (+0.0 / -0.0) for kOrdF32.
-template <int kOrd>
-__device__ __forceinline__ void ws_find(uint32_t* hist, uint32_t r, bool edge, uint32_t npad,
-                                        uint32_t& bin, uint32_t& below, uint32_t& cnt,
-                                        bool& special, uint32_t& z0, uint32_t& z1024) {
+// Scan of 2^B bins in value order (the orders above); lane l owns the
+// chunks 32 j + l, j < 2^B / 128.  Returns to every lane the raw bin holding
+// rank r, the count below it and its count, and zeroes the bins.  With `edge`
+// (floats), `special` reports a nonzero count in the first 4 bins of the value
+// order or more than npad in the last 4; zp / zn return the counts of raw bins
+// 0 and 2^(B-1) (the +0.0 and -0.0 bins) for kOrdF32.
+template <int kOrd, int B>
+__device__ __forceinline__ void bin_find(uint32_t* hist, uint32_t r, bool edge, uint32_t npad,
+                                         uint32_t& bin, uint32_t& below, uint32_t& cnt,
+                                         bool& special, uint32_t& zp, uint32_t& zn) {
+  constexpr int NG = (1 << B) / 128;  // groups of 128 bins = chunks per lane
+  constexpr int HG = NG / 2;
+  static_assert(kOrd == kOrdPlain || NG >= 2, "value orders split the groups by sign");
   const int lane = threadIdx.x & 31;
   uint4* hp = reinterpret_cast<uint4*>(hist) + lane;
-  uint32_t ls[16];
+  uint32_t ls[NG];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < NG; ++j) {
     const uint4 h = hp[32 * j];
     ls[j] = h.x + h.y + h.z + h.w;
   }
   if (kOrd == kOrdF32) {
-    z0 = hist[0];
-    z1024 = hist[1024];
+    zp = hist[0];
+    zn = hist[1 << (B - 1)];
   }
   bool sp = false;
-  if (kOrd == kOrdF32 && edge && lane == 31) sp = ls[15] != 0u || ls[7] != npad;
+  if (kOrd == kOrdF32 && edge && lane == 31) sp = ls[NG - 1] != 0u || ls[HG - 1] != npad;
   special = __any_sync(0xffffffffu, sp);
-  // the group holding rank r, walking the groups in value order
   uint32_t cum = 0, gbelow = 0;
   int J = -1;
 #pragma unroll
-  for (int g = 0; g < 16; ++g) {
-    const int j = kOrd == kOrdPlain ? g : (kOrd == kOrdF32 ? (g < 8 ? 15 - g : g - 8)
-                                                           : (g < 8 ? g + 8 : g - 8));
+  for (int g = 0; g < NG; ++g) {
+    const int j = kOrd == kOrdPlain ? g : (kOrd == kOrdF32 ? (g < HG ? NG - 1 - g : g - HG)
+                                                           : (g < HG ? g + HG : g - HG));
     const uint32_t G = __reduce_add_sync(0xffffffffu, ls[j]);
     if (J < 0 && r < cum + G) {
       J = j;
@@ -556,11 +556,10 @@ __device__ __forceinline__ void ws_find(uint32_t* hist, uint32_t r, bool edge, u
     cum += G;
   }
   if (J < 0) J = 0;  // r beyond the total: not reached for a valid rank
-  const bool desc = kOrd == kOrdF32 && J >= 8;
+  const bool desc = kOrd == kOrdF32 && J >= HG;
   const uint4 h = hp[32 * J];
   const uint32_t c[4] = {desc ? h.w : h.x, desc ? h.z : h.y, desc ? h.y : h.z, desc ? h.x : h.w};
   const uint32_t tot = c[0] + c[1] + c[2] + c[3];
-  // inclusive prefix over the lanes in value order (lane 31 first when descending)
   uint32_t inc = tot;
   if (desc) {
 #pragma unroll
@@ -597,9 +596,9 @@ __device__ __forceinline__ void ws_find(uint32_t* hist, uint32_t r, bool edge, u
     pbl = gbelow + acc;
     pc = cw;
   }
-  __syncwarp();  // every lane's reads (z0 / z1024 included) before the clear
+  __syncwarp();  // every lane's reads (zp / zn included) before the clear
 #pragma unroll
-  for (int j = 0; j < 16; ++j) hp[32 * j] = make_uint4(0, 0, 0, 0);
+  for (int j = 0; j < NG; ++j) hp[32 * j] = make_uint4(0, 0, 0, 0);
   bin = __shfl_sync(0xffffffffu, pb, ol < 0 ? 0 : ol);
   below = __shfl_sync(0xffffffffu, pbl, ol < 0 ? 0 : ol);
   cnt = __shfl_sync(0xffffffffu, pc, ol < 0 ? 0 : ol);
@@ -708,7 +707,7 @@ median_ws_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restr
     const uint4* R4 = reinterpret_cast<const uint4*>(S.raw[cw]);
     uint32_t s, below, cnt, z0 = 0, z1024 = 0;
     bool special;
-    ws_find<kOrd>(H, k, kF, npad, s, below, cnt, special, z0, z1024);
+    bin_find<kOrd, 11>(H, k, kF, npad, s, below, cnt, special, z0, z1024);
     bool done = false;
     if (kF && special) {
       // a NaN or an infinity is present: the first NaN (in index order) decides
@@ -767,7 +766,7 @@ median_ws_kernel(const T* __restrict__ x, T* __restrict__ vals, int64_t* __restr
         __syncwarp();
         uint32_t bb, bl, d0, d1;
         bool unused;
-        ws_find<kOrdPlain>(H, r, false, 0, bb, bl, cnt, unused, d0, d1);
+        bin_find<kOrdPlain, 11>(H, r, false, 0, bb, bl, cnt, unused, d0, d1);
         r -= bl;
         P |= bb << sh;
         Mk |= dm << sh;
@@ -915,96 +914,6 @@ struct __align__(16) WarpSmem {
   uint32_t ccount;
   uint32_t pad_[3];
 };
-
-// Scan of 2^B bins in value order (the orders of ws_find); lane l owns the
-// chunks 32 j + l, j < 2^B / 128.  Returns to every lane the raw bin holding
-// rank r, the count below it and its count, and zeroes the bins.  With `edge`
-// (floats), `special` reports a nonzero count in the first 4 bins of the value
-// order or more than npad in the last 4; zp / zn return the counts of raw bins
-// 0 and 2^(B-1) (the +0.0 and -0.0 bins) for kOrdF32.
-template <int kOrd, int B>
-__device__ __forceinline__ void bin_find(uint32_t* hist, uint32_t r, bool edge, uint32_t npad,
-                                         uint32_t& bin, uint32_t& below, uint32_t& cnt,
-                                         bool& special, uint32_t& zp, uint32_t& zn) {
-  constexpr int NG = (1 << B) / 128;  // groups of 128 bins = chunks per lane
-  constexpr int HG = NG / 2;
-  static_assert(kOrd == kOrdPlain || NG >= 2, "value orders split the groups by sign");
-  const int lane = threadIdx.x & 31;
-  uint4* hp = reinterpret_cast<uint4*>(hist) + lane;
-  uint32_t ls[NG];
-#pragma unroll
-  for (int j = 0; j < NG; ++j) {
-    const uint4 h = hp[32 * j];
-    ls[j] = h.x + h.y + h.z + h.w;
-  }
-  if (kOrd == kOrdF32) {
-    zp = hist[0];
-    zn = hist[1 << (B - 1)];
-  }
-  bool sp = false;
-  if (kOrd == kOrdF32 && edge && lane == 31) sp = ls[NG - 1] != 0u || ls[HG - 1] != npad;
-  special = __any_sync(0xffffffffu, sp);
-  uint32_t cum = 0, gbelow = 0;
-  int J = -1;
-#pragma unroll
-  for (int g = 0; g < NG; ++g) {
-    const int j = kOrd == kOrdPlain ? g : (kOrd == kOrdF32 ? (g < HG ? NG - 1 - g : g - HG)
-                                                           : (g < HG ? g + HG : g - HG));
-    const uint32_t G = __reduce_add_sync(0xffffffffu, ls[j]);
-    if (J < 0 && r < cum + G) {
-      J = j;
-      gbelow = cum;
-    }
-    cum += G;
-  }
-  if (J < 0) J = 0;  // r beyond the total: not reached for a valid rank
-  const bool desc = kOrd == kOrdF32 && J >= HG;
-  const uint4 h = hp[32 * J];
-  const uint32_t c[4] = {desc ? h.w : h.x, desc ? h.z : h.y, desc ? h.y : h.z, desc ? h.x : h.w};
-  const uint32_t tot = c[0] + c[1] + c[2] + c[3];
-  uint32_t inc = tot;
-  if (desc) {
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_down_sync(0xffffffffu, inc, o);
-      if (lane + o < 32) inc += y;
-    }
-  } else {
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += y;
-    }
-  }
-  const uint32_t rr = r - gbelow;
-  const uint32_t exc = inc - tot;
-  const bool own = exc <= rr && rr < inc;
-  const int ol = __ffs(__ballot_sync(0xffffffffu, own)) - 1;
-  uint32_t pb = 0, pbl = 0, pc = 0;
-  if (own) {
-    uint32_t acc = exc;
-    int w = 0;
-#pragma unroll
-    for (int j = 0; j < 3; ++j)
-      if (w == j && rr >= acc + c[j]) {
-        acc += c[j];
-        w = j + 1;
-      }
-    uint32_t cw = c[0];
-#pragma unroll
-    for (int j = 1; j < 4; ++j)
-      if (w == j) cw = c[j];
-    pb = 128u * J + 4u * lane + (desc ? 3 - w : w);
-    pbl = gbelow + acc;
-    pc = cw;
-  }
-  __syncwarp();  // every lane's reads (zp / zn included) before the clear
-#pragma unroll
-  for (int j = 0; j < NG; ++j) hp[32 * j] = make_uint4(0, 0, 0, 0);
-  bin = __shfl_sync(0xffffffffu, pb, ol < 0 ? 0 : ol);
-  below = __shfl_sync(0xffffffffu, pbl, ol < 0 ? 0 : ol);
-  cnt = __shfl_sync(0xffffffffu, pc, ol < 0 ? 0 : ol);
-}
 
 // value-order position of raw bin s of 2^B (= the top B bits of the key)
 template <typename T, int B>
