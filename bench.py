@@ -422,7 +422,12 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
                                                                       srcv[:sub], red,
                                                                       include_self=inc),
                                         sb, "GB/s", "first 2^20 of 2^24 index/src elements")
-                    launches = 1 + (0 if (red in ("sum", "prod") and inc) else 2)
+                    if red == "prod":
+                        # destination binning: count, pairs, reduce (+ init and
+                        # finalize of the cells without include_self)
+                        launches = 3 if inc else 5
+                    else:
+                        launches = 1 if (red == "sum" and inc) else 3
                     res[name] = hbm_entry(name, SCATTER_BYTES, ms, K, launches, hbm, src, traffic,
                                           cpu)
         if want("scatter_uniform_int32_sum"):
