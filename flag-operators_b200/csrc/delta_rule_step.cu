@@ -144,15 +144,22 @@ extern "C" int fo_gdr_fwd_stepwise(const void* q, const void* k, const void* v, 
   fo::clear_error();
   FO_CHECK_ARG(B >= 0 && H >= 0 && L >= 0, "chunk_gated_delta_rule: negative size");
   if (B * H == 0) return FO_OK;
-  FO_CHECK_ARG(q && k && v && beta && g && o, "chunk_gated_delta_rule: null pointer");
   if (L == 0) {
+    // no tokens: the final state is the initial one (the empty q, k, v, o may
+    // have null data pointers)
+    cudaError_t e = cudaSuccess;
     if (hT && h0)
-      cudaMemcpyAsync(hT, h0, B * H * D * D * sizeof(float), cudaMemcpyDeviceToDevice,
-                      fo::as_stream(stream));
+      e = cudaMemcpyAsync(hT, h0, B * H * D * D * sizeof(float), cudaMemcpyDeviceToDevice,
+                          fo::as_stream(stream));
     else if (hT)
-      cudaMemsetAsync(hT, 0, B * H * D * D * sizeof(float), fo::as_stream(stream));
+      e = cudaMemsetAsync(hT, 0, B * H * D * D * sizeof(float), fo::as_stream(stream));
+    if (e != cudaSuccess) {
+      fo::set_error("chunk_gated_delta_rule: %s", cudaGetErrorString(e));
+      return FO_ECUDA;
+    }
     return FO_OK;
   }
+  FO_CHECK_ARG(q && k && v && beta && g && o, "chunk_gated_delta_rule: null pointer");
   return fo::gdr_stepwise(q, k, v, beta, g, h0, o, hT, B, H, L, D, dtype, gate_dtype,
                           fo::as_stream(stream), nullptr);
 }

@@ -1206,17 +1206,24 @@ extern "C" int fo_gdr_fwd(const void* q, const void* k, const void* v, const voi
     return FO_EUNSUPPORTED;
   }
   if (B * H == 0) return FO_OK;
-  FO_CHECK_ARG(q && k && v && beta && g && o, "chunk_gated_delta_rule: null pointer");
   FO_CHECK_ARG(!(h0 && hT && (const void*)h0 == (const void*)hT),
                "chunk_gated_delta_rule: initial and final state must not alias");
   cudaStream_t st = as_stream(stream);
   if (L == 0) {
+    // no tokens: the final state is the initial one (the empty q, k, v, o may
+    // have null data pointers)
+    cudaError_t e = cudaSuccess;
     if (hT && h0)
-      cudaMemcpyAsync(hT, h0, B * H * D * D * sizeof(float), cudaMemcpyDeviceToDevice, st);
+      e = cudaMemcpyAsync(hT, h0, B * H * D * D * sizeof(float), cudaMemcpyDeviceToDevice, st);
     else if (hT)
-      cudaMemsetAsync(hT, 0, B * H * D * D * sizeof(float), st);
+      e = cudaMemsetAsync(hT, 0, B * H * D * D * sizeof(float), st);
+    if (e != cudaSuccess) {
+      set_error("chunk_gated_delta_rule: %s", cudaGetErrorString(e));
+      return FO_ECUDA;
+    }
     return FO_OK;
   }
+  FO_CHECK_ARG(q && k && v && beta && g && o, "chunk_gated_delta_rule: null pointer");
   if (gdr_tc_eligible(q, k, v, o, hT, D, dtype)) {
     int64_t need = 0;
     fo_gdr_workspace_bytes(B, H, L, D, dtype, &need);

@@ -80,6 +80,9 @@ _SIGS = {
                                      _c_void_p],
     "fo_gdr_fwd_stepwise": [_c_void_p] * 8 + [_i64, _i64, _i64, _i64, _int, _int, _c_void_p],
     "fo_gdr_timeouts": [_c_void_p],
+    "fo_gdr_bwd_workspace_bytes": [_i64, _i64, _i64, _i64, _i64p],
+    "fo_gdr_bwd": [_c_void_p] * 14 + [_i64, _i64, _i64, _i64, _int, _int, _c_void_p,
+                                      _i64, _c_void_p],
     "fo_median_timeouts": [_c_void_p],
     "fo_tc05_selftest": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _int, _int, _c_void_p],
 }

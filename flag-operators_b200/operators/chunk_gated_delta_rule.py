@@ -16,6 +16,13 @@ a head whose fp16 operands would leave the fp16 range is recomputed in the same
 call by the fp32 per-step kernel, so finite inputs give finite outputs.  fp32
 inputs run the per-step kernel (csrc/delta_rule_step.cu).  _ref_forward is kept importable, as the reference's
 tests import it; it is the reference's sequential fp32 loop on CPU tensors.
+
+Backward: when autograd needs a gradient of q, k, v, beta, g or initial_state,
+the call goes through an autograd Function whose backward is the fp32 CUDA-core
+kernel of csrc/delta_rule_bwd.cu (fo_gdr_bwd).  Its gradients are those torch
+autograd gives through the reference's CPU loop (the reference itself has no
+backward).  Without a gradient to compute, nothing is saved and the forward
+runs as before.
 """
 from __future__ import annotations
 
@@ -40,6 +47,63 @@ def _check_inputs(q, k, v, beta, g):
     return B, H, L, D
 
 
+def _forward(q, k, v, beta, g, h0, output_final_state):
+    """o (and the fp32 final state) through fo_gdr_fwd; inputs already checked."""
+    B, H, L, D = q.shape
+    o = torch.empty_like(q)
+    hT = torch.empty(B, H, D, D, dtype=torch.float32, device=q.device) \
+        if output_final_state else None
+    nbytes = ctypes.c_int64(0)
+    _lib.call("fo_gdr_workspace_bytes", B, H, L, D, _lib.dtype_code(q.dtype),
+              ctypes.byref(nbytes))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device) if nbytes.value else None
+    _lib.call("fo_gdr_fwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(beta), _lib.ptr(g),
+              _lib.ptr(h0), _lib.ptr(o), _lib.ptr(hT), B, H, L, D, _lib.dtype_code(q.dtype),
+              _lib.dtype_code(beta.dtype), _lib.ptr(ws), nbytes.value, _lib.stream_of(q))
+    return o, hT
+
+
+def _backward(q, k, v, beta, g, h0, do, dhT, need_dh0):
+    """(dq, dk, dv, dbeta, dg, dh0) through fo_gdr_bwd; do / dhT may be None."""
+    B, H, L, D = q.shape
+    do = torch.zeros_like(q) if do is None else do.to(q.dtype).contiguous()
+    if dhT is not None:
+        dhT = dhT.to(torch.float32).contiguous()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dbeta, dg = torch.empty_like(beta), torch.empty_like(beta)
+    dh0 = torch.empty(B, H, D, D, dtype=torch.float32, device=q.device) if need_dh0 else None
+    nbytes = ctypes.c_int64(0)
+    _lib.call("fo_gdr_bwd_workspace_bytes", B, H, L, D, ctypes.byref(nbytes))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device) if nbytes.value else None
+    _lib.call("fo_gdr_bwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(beta), _lib.ptr(g),
+              _lib.ptr(h0), _lib.ptr(do), _lib.ptr(dhT), _lib.ptr(dq), _lib.ptr(dk),
+              _lib.ptr(dv), _lib.ptr(dbeta), _lib.ptr(dg), _lib.ptr(dh0), B, H, L, D,
+              _lib.dtype_code(q.dtype), _lib.dtype_code(beta.dtype), _lib.ptr(ws), nbytes.value,
+              _lib.stream_of(q))
+    return dq, dk, dv, dbeta, dg, dh0
+
+
+class _GatedDeltaRule(torch.autograd.Function):
+    """Forward through fo_gdr_fwd, backward through fo_gdr_bwd (inputs are saved;
+    the backward recomputes the states from them)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, beta, g, h0, output_final_state):
+        o, hT = _forward(q, k, v, beta, g, h0, output_final_state)
+        ctx.save_for_backward(q, k, v, beta, g, h0)
+        ctx.set_materialize_grads(False)
+        if output_final_state:
+            return o, hT
+        return o
+
+    @staticmethod
+    def backward(ctx, do, dhT=None):
+        q, k, v, beta, g, h0 = ctx.saved_tensors
+        dq, dk, dv, dbeta, dg, dh0 = _backward(q, k, v, beta, g, h0, do, dhT,
+                                               h0 is not None and ctx.needs_input_grad[5])
+        return dq, dk, dv, dbeta, dg, dh0, None
+
+
 def chunk_gated_delta_rule(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -50,7 +114,7 @@ def chunk_gated_delta_rule(
     initial_state: torch.Tensor | None = None,
     output_final_state: bool = False,
 ):
-    """Gated delta rule forward (chunk_gated_delta_rule.py:208-268)."""
+    """Gated delta rule forward (chunk_gated_delta_rule.py:208-268), differentiable."""
     logger.debug("FLAG-OPS CHUNK_GATED_DELTA_RULE")
     _lib.require_cuda(q, "chunk_gated_delta_rule")
     B, H, L, D = _check_inputs(q, k, v, beta, g)
@@ -60,21 +124,15 @@ def chunk_gated_delta_rule(
         g = g.to(beta.dtype)
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     beta, g = beta.contiguous(), g.contiguous()
-    o = torch.empty_like(q)
     h0 = None
     if initial_state is not None:
         assert initial_state.shape == (B, H, D, D), (
             f"initial_state shape {tuple(initial_state.shape)}, expected ({B},{H},{D},{D})")
         h0 = initial_state.to(device=q.device, dtype=torch.float32).contiguous()
-    hT = torch.empty(B, H, D, D, dtype=torch.float32, device=q.device) \
-        if output_final_state else None
-    nbytes = ctypes.c_int64(0)
-    _lib.call("fo_gdr_workspace_bytes", B, H, L, D, _lib.dtype_code(q.dtype),
-              ctypes.byref(nbytes))
-    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device) if nbytes.value else None
-    _lib.call("fo_gdr_fwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(beta), _lib.ptr(g),
-              _lib.ptr(h0), _lib.ptr(o), _lib.ptr(hT), B, H, L, D, _lib.dtype_code(q.dtype),
-              _lib.dtype_code(beta.dtype), _lib.ptr(ws), nbytes.value, _lib.stream_of(q))
+    if torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (q, k, v, beta, g, h0)):
+        return _GatedDeltaRule.apply(q, k, v, beta, g, h0, output_final_state)
+    o, hT = _forward(q, k, v, beta, g, h0, output_final_state)
     if output_final_state:
         return o, hT
     return o

@@ -359,6 +359,30 @@ FO_API int fo_gdr_fwd_stepwise(const void* q, const void* k, const void* v,
  * outputs incomplete).  Synchronous read of a device counter. */
 FO_API int fo_gdr_timeouts(unsigned int* count);
 
+/*
+ * Backward of the same recurrence: gradients of a loss L(o, h_T) given
+ * d_o = dL/do ([B, H, L, D], dtype) and dhT = dL/dh_T ([B, H, D, D] fp32, or
+ * NULL when the final state is not used).  Writes dq, dk, dv ([B, H, L, D],
+ * dtype), dbeta, dg ([B, H, L], gate_dtype) and, when dh0 is not NULL, the
+ * gradient of the initial state ([B, H, D, D] fp32); h0 is the forward's
+ * initial state or NULL.  Computed in fp32 on the CUDA cores from the inputs
+ * alone (it does not read the forward's outputs): the states are recomputed
+ * from checkpoints every 32 steps kept in the workspace
+ * (fo_gdr_bwd_workspace_bytes: B*H*(ceil(L/32) + min(L, 32))*D*D*4 bytes,
+ * 16-byte aligned, as h0, dhT and dh0 must be).  Deterministic (fixed-order
+ * sums).  D in {16, 32, 64, 128}.
+ * The reference has no backward kernel: its CPU path
+ * (_ref_forward, operators/chunk_gated_delta_rule.py:286-310) is differentiated
+ * by torch autograd, and these are those gradients.
+ */
+FO_API int fo_gdr_bwd_workspace_bytes(int64_t B, int64_t H, int64_t L, int64_t D,
+                                      int64_t* bytes);
+FO_API int fo_gdr_bwd(const void* q, const void* k, const void* v, const void* beta,
+                      const void* g, const float* h0, const void* d_o, const float* dhT,
+                      void* dq, void* dk, void* dv, void* dbeta, void* dg, float* dh0,
+                      int64_t B, int64_t H, int64_t L, int64_t D, int dtype, int gate_dtype,
+                      void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Number of hand-off waits of the producer/consumer median kernel (rows of
  * 1024 < N <= 2048) that ran out of polls since the library was loaded (0 in a
  * healthy run; a timed-out CTA stops and leaves its remaining rows unwritten).

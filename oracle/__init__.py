@@ -24,6 +24,8 @@ from .ops import (  # noqa: F401
     fused_cross_entropy,
     fused_cross_entropy_grad,
     delta_rule_forward,
+    delta_rule_grads,
+    delta_rule_backward,
     ce_shard_stats,
     ce_shard_combine,
     ce_rows_partial,

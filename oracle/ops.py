@@ -180,6 +180,91 @@ def delta_rule_forward(q, k, v, beta, g, initial_state=None, output_final_state=
     return o
 
 
+def delta_rule_grads(q, k, v, beta, g, do, initial_state=None, dhT=None):
+    """Gradients of the reference's CPU recurrence by torch autograd.
+
+    The reference's CPU branch (_ref_forward, chunk_gated_delta_rule.py:286-310) is
+    plain differentiable torch; the reference ships no backward of its own, so the
+    gradients it defines are autograd's through that loop.  The loop below is the
+    same statement (fp32 state, inputs read as fp32, gates promoted against the
+    fp32 state), with o_t kept in fp32 (the cast to q's dtype at :308 has an
+    identity backward).  Loss = sum(o * do) + sum(h_T * dhT); returns fp32
+    gradients {q, k, v, beta, g, initial_state}.
+    """
+    leaves = [_cpu(t).float().clone().requires_grad_(True) for t in (q, k, v, beta, g)]
+    qf, kf, vf, bf, gf = leaves
+    B, H, L, D = qf.shape
+    if initial_state is None:
+        h0 = torch.zeros(B, H, D, D, dtype=torch.float32, requires_grad=True)
+    else:
+        h0 = _cpu(initial_state).float().clone().requires_grad_(True)
+    h = h0
+    outs = []
+    for t in range(L):
+        k_t = kf[:, :, t, :]
+        delta = vf[:, :, t, :] - (h @ k_t.unsqueeze(-1)).squeeze(-1)
+        h = (gf[:, :, t, None, None] * h
+             + bf[:, :, t, None, None] * (delta.unsqueeze(-1) * k_t.unsqueeze(-2)))
+        outs.append((h @ qf[:, :, t, :].unsqueeze(-1)).squeeze(-1))
+    loss = torch.zeros((), dtype=torch.float32)
+    if L:
+        loss = loss + (torch.stack(outs, dim=2) * _cpu(do).float()).sum()
+    if dhT is not None:
+        loss = loss + (h * _cpu(dhT).float()).sum()
+    if loss.requires_grad:
+        loss.backward()
+    names = ("q", "k", "v", "beta", "g")
+    res = {n: (x.grad if x.grad is not None else torch.zeros_like(x)) for n, x in zip(names, leaves)}
+    res["initial_state"] = h0.grad if h0.grad is not None else torch.zeros_like(h0)
+    return res
+
+
+def delta_rule_backward(q, k, v, beta, g, do, initial_state=None, dhT=None):
+    """The per-step reverse recurrence the CUDA backward implements, in float64.
+
+    With h_{t-1} the state before step t, delta_t = v_t - h_{t-1} k_t and G the
+    gradient of the loss with respect to h_t (do_t q_t^T plus what flows back from
+    h_{t+1}), differentiating h_t = g_t h_{t-1} + beta_t delta_t k_t^T and
+    o_t = h_t q_t gives, per step in reverse:
+      gk = G k_t;  dv_t = beta_t gk;  dbeta_t = gk . delta_t;  dg_t = <G, h_{t-1}>
+      dq_t = h_t^T do_t = g_t h_{t-1}^T do_t + beta_t (delta_t . do_t) k_t
+      dk_t = beta_t (G^T delta_t - h_{t-1}^T gk)
+      G <- g_t G - beta_t gk k_t^T          (the gradient with respect to h_{t-1})
+    and the initial state's gradient is the final G.  Checked against
+    delta_rule_grads (autograd) by the CPU tests.
+    """
+    q, k, v, beta, g, do = (_cpu(t).double() for t in (q, k, v, beta, g, do))
+    B, H, L, D = q.shape
+    h = (torch.zeros(B, H, D, D, dtype=torch.float64) if initial_state is None
+         else _cpu(initial_state).double().clone())
+    hs = []
+    for t in range(L):
+        hs.append(h)
+        k_t = k[:, :, t]
+        delta = v[:, :, t] - (h @ k_t[..., None])[..., 0]
+        h = g[:, :, t, None, None] * h + beta[:, :, t, None, None] * (delta[..., None]
+                                                                         * k_t[..., None, :])
+    G = (torch.zeros(B, H, D, D, dtype=torch.float64) if dhT is None
+         else _cpu(dhT).double().clone())
+    dq, dk, dv = torch.zeros_like(q), torch.zeros_like(k), torch.zeros_like(v)
+    dbeta, dg = torch.zeros_like(beta), torch.zeros_like(g)
+    for t in reversed(range(L)):
+        hp, k_t, q_t, do_t = hs[t], k[:, :, t], q[:, :, t], do[:, :, t]
+        b_t, g_t = beta[:, :, t, None], g[:, :, t, None]
+        G = G + do_t[..., None] * q_t[..., None, :]
+        gk = (G @ k_t[..., None])[..., 0]
+        delta = v[:, :, t] - (hp @ k_t[..., None])[..., 0]
+        dv[:, :, t] = b_t * gk
+        dbeta[:, :, t] = (gk * delta).sum(-1)
+        dg[:, :, t] = (G * hp).sum((-1, -2))
+        dq[:, :, t] = (g_t * (hp.transpose(-1, -2) @ do_t[..., None])[..., 0]
+                       + b_t * (delta * do_t).sum(-1, keepdim=True) * k_t)
+        dk[:, :, t] = b_t * ((G.transpose(-1, -2) @ delta[..., None])[..., 0]
+                             - (hp.transpose(-1, -2) @ gk[..., None])[..., 0])
+        G = g_t[..., None] * G - b_t[..., None] * gk[..., None] * k_t[..., None, :]
+    return {"q": dq, "k": dk, "v": dv, "beta": dbeta, "g": dg, "initial_state": G}
+
+
 # ---------------------------------------------------------------------------
 # vocabulary-sharded cross-entropy: statement of the sharded algorithm on CPU
 # (used by the multi-process tests to check the host logic and the combine rule;

@@ -129,3 +129,29 @@ def test_delta_rule_checks():
     _lib.call("fo_gdr_fwd", *([None] * 8), 0, 4, 16, 128, BF16, BF16, None, 0, None)  # no heads
     with pytest.raises(ValueError, match="N, K in"):
         _lib.call("fo_tc05_selftest", DUMMY, DUMMY, DUMMY, 32, 64, 0, 0, None)
+
+
+def test_delta_rule_backward_checks():
+    bwd_args = lambda B, H, L, D, ws, nbytes: (  # noqa: E731
+        *([DUMMY] * 5), None, DUMMY, None, *([DUMMY] * 5), None, B, H, L, D, BF16, BF16, ws,
+        nbytes, None)
+    with pytest.raises(RuntimeError, match="D=100"):
+        _lib.call("fo_gdr_bwd", *bwd_args(1, 1, 16, 100, DUMMY, 1 << 30))
+    with pytest.raises(ValueError, match="negative size"):
+        _lib.call("fo_gdr_bwd", *bwd_args(-1, 1, 16, 128, DUMMY, 1 << 30))
+    _lib.call("fo_gdr_bwd", *bwd_args(0, 4, 16, 128, None, 0))  # no heads: nothing to do
+    # workspace: a checkpoint per 32 steps plus one chunk of states, per head
+    n = ctypes.c_int64(-1)
+    _lib.call("fo_gdr_bwd_workspace_bytes", 2, 3, 70, 64, ctypes.byref(n))
+    assert n.value == 6 * (3 + 32) * 64 * 64 * 4
+    _lib.call("fo_gdr_bwd_workspace_bytes", 1, 1, 5, 16, ctypes.byref(n))
+    assert n.value == (1 + 5) * 16 * 16 * 4
+    with pytest.raises(RuntimeError, match="D=48"):
+        _lib.call("fo_gdr_bwd_workspace_bytes", 1, 1, 5, 48, ctypes.byref(n))
+    need = 6 * (3 + 32) * 64 * 64 * 4
+    with pytest.raises(RuntimeError, match="workspace of"):
+        _lib.call("fo_gdr_bwd", *bwd_args(2, 3, 70, 64, DUMMY, need - 1))
+    with pytest.raises(ValueError, match="16-byte aligned"):
+        _lib.call("fo_gdr_bwd", *bwd_args(2, 3, 70, 64, DUMMY + 4, need))
+    with pytest.raises(ValueError, match="null pointer"):
+        _lib.call("fo_gdr_bwd", *([None] * 14), 1, 1, 8, 16, BF16, BF16, DUMMY, need, None)

@@ -165,3 +165,25 @@ def test_rms_norm_backward_oracle_matches_the_analytic_gradient():
     dw_ref = (dyd * xd * inv).sum(axis=0)
     np.testing.assert_allclose(dx.numpy(), dx_ref, rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(dw.numpy(), dw_ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("with_h0", [False, True])
+@pytest.mark.parametrize("with_dhT", [False, True])
+def test_delta_rule_backward_restatement_matches_autograd(with_h0, with_dhT):
+    """The per-step reverse recurrence the CUDA backward implements equals torch
+    autograd through the reference's loop (the gradients the reference defines)."""
+    gen = torch.Generator().manual_seed(7)
+    B, H, L, D = 2, 2, 37, 8
+    q, k, v, do = (torch.randn(B, H, L, D, generator=gen, dtype=torch.float64)
+                   for _ in range(4))
+    k = k / k.norm(dim=-1, keepdim=True)
+    beta = torch.sigmoid(torch.randn(B, H, L, generator=gen, dtype=torch.float64))
+    g = torch.sigmoid(torch.randn(B, H, L, generator=gen, dtype=torch.float64))
+    h0 = torch.randn(B, H, D, D, generator=gen, dtype=torch.float64) if with_h0 else None
+    dhT = torch.randn(B, H, D, D, generator=gen, dtype=torch.float64) if with_dhT else None
+    ref = oracle.delta_rule_grads(q, k, v, beta, g, do, h0, dhT)
+    got = oracle.delta_rule_backward(q, k, v, beta, g, do, h0, dhT)
+    for name, r in ref.items():
+        r = r.double()
+        scale = r.abs().max().item()
+        assert (got[name] - r).abs().max().item() <= 1e-5 * scale + 1e-12, name
