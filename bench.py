@@ -537,6 +537,53 @@ def run_per_op(args, dev, peaks, traffic, do_cpu, dist=None):
         e["parity"] = "ok" if (ok1 and ok2) else f"FAIL head 0: o {d1}; state {d2}"
         res["chunk_gated_delta_rule_d64"] = e
         del dins, o2
+
+    if want("chunk_gated_delta_rule_bwd"):
+        # backward at the benchmark shape: one fo_gdr_bwd call (the kernel the
+        # autograd Function runs) = dq, dk, dv, dbeta, dg from q, k, v, beta, g, do;
+        # fp32 CUDA-core reverse scan with the states recomputed from 16-step
+        # checkpoints
+        from operators.chunk_gated_delta_rule import _backward
+        ins = delta_inputs()
+        dins = [t.to(dev) for t in ins]
+        do_c = torch.randn(ins[0].shape, generator=_gen(1)).bfloat16()
+        do_d = do_c.to(dev)
+        ms = time_steps(lambda: _backward(*dins, None, do_d, None, False), K, W, flush, dist)
+        t = ms / K / 1e3
+        Bd, Hd, Ld, Dd = dins[0].shape
+        n = Bd * Hd * Ld * Dd
+        # read q, k, v, do and the gates; write dq, dk, dv and the gate gradients
+        nbytes = 7 * n * 2 + 4 * Bd * Hd * Ld * 2
+        e = hbm_entry("chunk_gated_delta_rule_bwd", nbytes, ms, K, 1, hbm, src, traffic)
+        e.update({"metric": "chunk_gated_delta_rule backward tokens/s",
+                  "value": round(Bd * Ld / t, 1), "unit": "tokens/s (B*L per second)",
+                  "fp32_flops_per_call": 22 * Dd * Dd * Bd * Hd * Ld,
+                  "note": "per-step fp32 CUDA-core kernel (no chunked tensor-core backward yet)"})
+        if do_cpu:
+            # autograd through the reference loop, L=64 prefix of all heads, scaled
+            # linearly to L=8192
+            Ls = 64
+            sub = [(x[:, :, :Ls] if x.dim() == 3 else x[:, :, :Ls, :]).contiguous() for x in ins]
+            tc = cpu_time(lambda: oracle.delta_rule_grads(*sub, do_c[:, :, :Ls]), min_reps=2,
+                          min_seconds=0.5)
+            e["cpu_baseline"] = {"value": round(Bd * Ld / (tc * Ld / Ls), 3), "unit": "tokens/s",
+                                 "cores": torch.get_num_threads(), "kind": "port",
+                                 "cpu": cpu_model(),
+                                 "sample": f"autograd through the reference loop, all {Bd}x{Hd} "
+                                           f"heads, L={Ls} prefix, scaled linearly to L={Ld}"}
+        # parity: head 0, first 256 tokens, against autograd through the reference loop
+        Lp = 256
+        sl = [(x[:1, :1, :Lp] if x.dim() == 3 else x[:1, :1, :Lp, :]).contiguous() for x in ins]
+        got = _backward(*[x.to(dev) for x in sl], None, do_c[:1, :1, :Lp].to(dev), None, False)
+        ref = oracle.delta_rule_grads(*sl, do_c[:1, :1, :Lp])
+        bad = []
+        for name, gr in zip(("q", "k", "v", "beta", "g"), got[:5]):
+            ok, d = _delta_close(gr, ref[name])
+            if not ok:
+                bad.append(f"d{name}: {d}")
+        e["parity"] = "ok" if not bad else "FAIL head 0: " + "; ".join(bad)
+        res["chunk_gated_delta_rule_bwd"] = e
+        del dins, do_d
     return res
 
 

@@ -14,12 +14,18 @@
 //
 // The recurrence is separable by state row: row i of h and of G evolves on its
 // own, and only dq, dk, dbeta and dg sum over rows.  One CTA per (batch, head),
-// 8 threads per state row, D / 8 columns per thread, everything in fp32:
-//   1. a forward pass over the sequence writes the state at every 32-step
+// 8 threads per state row, D / 8 columns per thread (thread s of a row holds
+// columns s, s + 8, s + 16, ..., so that the 8 lanes of a row read 8
+// consecutive floats of a staged k or q row: no shared-memory bank conflicts),
+// everything in fp32:
+//   1. a forward pass over the sequence writes the state at every 16-step
 //      checkpoint (workspace);
 //   2. chunks in reverse: stage the chunk's q, k, v, do, beta, g in shared
 //      memory, recompute its states from the checkpoint into a per-head scratch
-//      (each thread reads back only what it wrote), then run the reverse steps.
+//      (each thread reads back only what it wrote; 16 states of every head,
+//      128 MB at 128 heads of D = 128, mostly stay in L2), then run the reverse
+//      steps, each loading the next step's state as soon as the current one is
+//      dead so that the load overlaps the barrier and the block sums.
 //      Row dot products are reduced across a row's 8 lanes with shuffles; the
 //      column sums over rows (dq, dk) and the scalar sums (dbeta, dg) are
 //      reduced across a warp's four rows with shuffles, then across warps in a
@@ -31,7 +37,7 @@
 namespace fo {
 namespace {
 
-constexpr int kBwdChunk = 32;  // steps between state checkpoints
+constexpr int kBwdChunk = 16;  // steps between state checkpoints
 constexpr int kBwdTPR = 8;     // threads per state row
 
 template <int D>
@@ -118,7 +124,7 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   float* s_g = s_b + CH;         // [CH]
   float* s_red = s_g + CH;       // [2][NW][RED]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row = tid / kBwdTPR, c0 = (tid % kBwdTPR) * CPT;
+  const int row = tid / kBwdTPR, seg = tid % kBwdTPR;  // columns seg + kBwdTPR * c
   const int64_t head = blockIdx.x;
   const int64_t nch = (L + CH - 1) / CH;
   const int64_t chs = L < CH ? L : CH;  // scratch states per head
@@ -129,7 +135,15 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   const T* doh = dout + head * L * D;
   float* ck = ckpt + head * nch * DD;
   float* sc = scratch + head * chs * DD;
-  const int64_t my = (int64_t)row * D + c0;  // this thread's offset inside a [D, D] state
+  // this thread's CPT values inside a [D, D] state: in the workspace (checkpoints,
+  // scratch) as one contiguous segment, read back only by this thread; in the
+  // caller's row-major h0, dhT and dh0 at row * D + seg + kBwdTPR * c
+  const int64_t my = (int64_t)row * D + seg * CPT;
+  const int64_t mine = (int64_t)row * D + seg;
+  auto ld_cols = [&](const float* p, float* r) {
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) r[c] = p[mine + kBwdTPR * c];
+  };
 
   // chunk c's inputs into shared memory as fp32; returns its step count
   auto stage = [&](int64_t c, bool full) {
@@ -155,22 +169,22 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 
   // one forward step of this thread's row segment
   auto fwd_step = [&](float* h, int tl) {
-    const float* kr = s_k + tl * D + c0;
+    const float* kr = s_k + tl * D + seg;
     float r = 0.f;
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) r = fmaf(h[c], kr[c], r);
+    for (int c = 0; c < CPT; ++c) r = fmaf(h[c], kr[kBwdTPR * c], r);
     r = row_sum(r);
     const float bu = s_b[tl] * (s_v[tl * D + row] - r);
     const float gt = s_g[tl];
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) h[c] = fmaf(gt, h[c], bu * kr[c]);
+    for (int c = 0; c < CPT; ++c) h[c] = fmaf(gt, h[c], bu * kr[kBwdTPR * c]);
   };
 
   // ---- 1. forward: the state entering every chunk
   {
     float h[CPT];
     if (h0) {
-      ld_seg<CPT>(h0 + head * DD + my, h);
+      ld_cols(h0 + head * DD, h);
     } else {
 #pragma unroll
       for (int c = 0; c < CPT; ++c) h[c] = 0.f;
@@ -187,7 +201,7 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   // ---- 2. chunks in reverse
   float G[CPT];
   if (dhT) {
-    ld_seg<CPT>(dhT + head * DD + my, G);
+    ld_cols(dhT + head * DD, G);
   } else {
 #pragma unroll
     for (int c = 0; c < CPT; ++c) G[c] = 0.f;
@@ -207,20 +221,20 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
         fwd_step(h, tl);
       }
     }
+    float hp[CPT];  // the state before step tl
+    ld_seg<CPT>(sc + (n - 1) * DD + my, hp);
     for (int tl = n - 1; tl >= 0; --tl) {
       const int64_t t = c * CH + tl;
-      float hp[CPT];
-      ld_seg<CPT>(sc + tl * DD + my, hp);
-      const float* kr = s_k + tl * D + c0;
-      const float* qr = s_q + tl * D + c0;
+      const float* kr = s_k + tl * D + seg;
+      const float* qr = s_q + tl * D + seg;
       const float do_i = s_do[tl * D + row];
       const float bt = s_b[tl], gt = s_g[tl];
       float gk = 0.f, hk = 0.f, gh = 0.f;
 #pragma unroll
       for (int cc = 0; cc < CPT; ++cc) {
-        G[cc] = fmaf(do_i, qr[cc], G[cc]);
-        gk = fmaf(G[cc], kr[cc], gk);
-        hk = fmaf(hp[cc], kr[cc], hk);
+        G[cc] = fmaf(do_i, qr[kBwdTPR * cc], G[cc]);
+        gk = fmaf(G[cc], kr[kBwdTPR * cc], gk);
+        hk = fmaf(hp[cc], kr[kBwdTPR * cc], hk);
         gh = fmaf(G[cc], hp[cc], gh);
       }
       gk = row_sum(gk);
@@ -234,10 +248,11 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
         const float pq = warp_rows_sum(do_i * hp[cc]);
         const float pk = warp_rows_sum(fmaf(G[cc], delta, -gk * hp[cc]));
         if (lane < kBwdTPR) {
-          red[c0 + cc] = pq;
-          red[D + c0 + cc] = pk;
+          red[seg + kBwdTPR * cc] = pq;
+          red[D + seg + kBwdTPR * cc] = pk;
         }
       }
+      if (tl > 0) ld_seg<CPT>(sc + (tl - 1) * DD + my, hp);  // hp is dead from here on
       const float s_gd = warp_rows_sum(gk * delta);
       const float s_gh = warp_rows_sum(gh);
       const float s_dd = warp_rows_sum(do_i * delta);
@@ -247,7 +262,7 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
         red[2 * D + 2] = s_dd;
       }
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) G[cc] = fmaf(gt, G[cc], -bt * gk * kr[cc]);
+      for (int cc = 0; cc < CPT; ++cc) G[cc] = fmaf(gt, G[cc], -bt * gk * kr[kBwdTPR * cc]);
       __syncthreads();
       // the step's sums over all rows, warps added in a fixed order
       const float* rr = s_red + rb * NW * RED;
@@ -277,7 +292,10 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       rb ^= 1;
     }
   }
-  if (dh0) st_seg<CPT>(dh0 + head * DD + my, G);
+  if (dh0) {
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) dh0[head * DD + mine + kBwdTPR * c] = G[c];
+  }
 }
 
 template <typename T, typename Gt, int D>
@@ -346,7 +364,7 @@ int bwd_bad_dim(int64_t D) {
   return FO_EUNSUPPORTED;
 }
 
-// checkpoints (one state per 32 steps) + one chunk of recomputed states, per head
+// checkpoints (one state per 16 steps) + one chunk of recomputed states, per head
 int64_t bwd_workspace_floats(int64_t BH, int64_t L, int64_t D) {
   const int64_t nch = (L + kBwdChunk - 1) / kBwdChunk;
   const int64_t chs = L < kBwdChunk ? L : kBwdChunk;
@@ -400,10 +418,8 @@ extern "C" int fo_gdr_bwd(const void* q, const void* k, const void* v, const voi
                   (long long)workspace_bytes, (long long)need);
     return FO_EWORKSPACE;
   }
-  FO_CHECK_ARG(fo::aligned16(workspace) && (!h0 || fo::aligned16(h0)) &&
-                   (!dhT || fo::aligned16(dhT)) && (!dh0 || fo::aligned16(dh0)),
-               "chunk_gated_delta_rule backward: workspace and fp32 states must be 16-byte "
-               "aligned");
+  FO_CHECK_ARG(fo::aligned16(workspace),
+               "chunk_gated_delta_rule backward: the workspace must be 16-byte aligned");
   float* ckpt = static_cast<float*>(workspace);
   const int64_t nch = (L + fo::kBwdChunk - 1) / fo::kBwdChunk;
   float* scratch = ckpt + BH * nch * D * D;

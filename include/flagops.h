@@ -367,9 +367,9 @@ FO_API int fo_gdr_timeouts(unsigned int* count);
  * gradient of the initial state ([B, H, D, D] fp32); h0 is the forward's
  * initial state or NULL.  Computed in fp32 on the CUDA cores from the inputs
  * alone (it does not read the forward's outputs): the states are recomputed
- * from checkpoints every 32 steps kept in the workspace
- * (fo_gdr_bwd_workspace_bytes: B*H*(ceil(L/32) + min(L, 32))*D*D*4 bytes,
- * 16-byte aligned, as h0, dhT and dh0 must be).  Deterministic (fixed-order
+ * from checkpoints every 16 steps kept in the workspace
+ * (fo_gdr_bwd_workspace_bytes: B*H*(ceil(L/16) + min(L, 16))*D*D*4 bytes,
+ * 16-byte aligned).  Deterministic (fixed-order
  * sums).  D in {16, 32, 64, 128}.
  * The reference has no backward kernel: its CPU path
  * (_ref_forward, operators/chunk_gated_delta_rule.py:286-310) is differentiated

@@ -140,15 +140,15 @@ def test_delta_rule_backward_checks():
     with pytest.raises(ValueError, match="negative size"):
         _lib.call("fo_gdr_bwd", *bwd_args(-1, 1, 16, 128, DUMMY, 1 << 30))
     _lib.call("fo_gdr_bwd", *bwd_args(0, 4, 16, 128, None, 0))  # no heads: nothing to do
-    # workspace: a checkpoint per 32 steps plus one chunk of states, per head
+    # workspace: a checkpoint per 16 steps plus one chunk of states, per head
     n = ctypes.c_int64(-1)
     _lib.call("fo_gdr_bwd_workspace_bytes", 2, 3, 70, 64, ctypes.byref(n))
-    assert n.value == 6 * (3 + 32) * 64 * 64 * 4
+    assert n.value == 6 * (5 + 16) * 64 * 64 * 4
     _lib.call("fo_gdr_bwd_workspace_bytes", 1, 1, 5, 16, ctypes.byref(n))
     assert n.value == (1 + 5) * 16 * 16 * 4
     with pytest.raises(RuntimeError, match="D=48"):
         _lib.call("fo_gdr_bwd_workspace_bytes", 1, 1, 5, 48, ctypes.byref(n))
-    need = 6 * (3 + 32) * 64 * 64 * 4
+    need = 6 * (5 + 16) * 64 * 64 * 4
     with pytest.raises(RuntimeError, match="workspace of"):
         _lib.call("fo_gdr_bwd", *bwd_args(2, 3, 70, 64, DUMMY, need - 1))
     with pytest.raises(ValueError, match="16-byte aligned"):
