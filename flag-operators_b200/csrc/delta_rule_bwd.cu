@@ -14,10 +14,13 @@
 //
 // The recurrence is separable by state row: row i of h and of G evolves on its
 // own, and only dq, dk, dbeta and dg sum over rows.  One CTA per (batch, head),
-// 8 threads per state row, D / 8 columns per thread (thread s of a row holds
-// columns s, s + 8, s + 16, ..., so that the 8 lanes of a row read 8
-// consecutive floats of a staged k or q row: no shared-memory bank conflicts),
-// everything in fp32:
+// everything in fp32.  A thread holds two state rows (2p, 2p + 1) and D / 16 of
+// their columns (s, s + 16, s + 32, ...; the 16 lanes of a row pair read 16
+// consecutive floats of a staged k or q row: no shared-memory bank conflicts);
+// a warp holds two row pairs.  So a row dot product is a 4-level shuffle over 16
+// lanes, and a column sum over the warp's four rows is the thread's own two rows
+// plus one shuffle (these shuffles and the staged-row loads share the MIO pipe,
+// which bounds the step).
 //   1. a forward pass over the sequence writes the state at every 16-step
 //      checkpoint (workspace);
 //   2. chunks in reverse: stage the chunk's q, k, v, do, beta, g in shared
@@ -25,12 +28,11 @@
 //      (each thread reads back only what it wrote; 16 states of every head,
 //      128 MB at 128 heads of D = 128, mostly stay in L2), then run the reverse
 //      steps, each loading the next step's state as soon as the current one is
-//      dead so that the load overlaps the barrier and the block sums.
-//      Row dot products are reduced across a row's 8 lanes with shuffles; the
-//      column sums over rows (dq, dk) and the scalar sums (dbeta, dg) are
-//      reduced across a warp's four rows with shuffles, then across warps in a
-//      double-buffered shared-memory block in a fixed order, so one barrier per
-//      step and the result does not depend on scheduling.
+//      dead so that the load overlaps the barrier and the block sums.  The
+//      column sums (dq, dk) and scalar sums (dbeta, dg) of a step go through a
+//      double-buffered shared-memory block, one slot per warp, added over the
+//      warps in a fixed order: one barrier per step, and the result does not
+//      depend on scheduling.
 // No waits other than block barriers.
 #include "common.cuh"
 
@@ -38,14 +40,14 @@ namespace fo {
 namespace {
 
 constexpr int kBwdChunk = 16;  // steps between state checkpoints
-constexpr int kBwdTPR = 8;     // threads per state row
+constexpr int kBwdSeg = 16;    // lanes per row pair (column stride of a thread)
 
 template <int D>
 struct BwdCfg {
-  static constexpr int CPT = D / kBwdTPR;  // columns per thread
-  static constexpr int NT = D * kBwdTPR;   // threads per CTA
-  static constexpr int NW = NT / 32;       // warps
-  static constexpr int RED = 2 * D + 4;    // floats per warp in a reduction buffer
+  static constexpr int CPT = D / kBwdSeg;    // columns per thread (of each of its two rows)
+  static constexpr int NT = (D / 2) * kBwdSeg;  // threads per CTA (= 8 D)
+  static constexpr int NW = NT / 32;         // warps
+  static constexpr int RED = 2 * D + 4;      // floats per warp in a reduction buffer
 };
 
 template <int D>
@@ -90,19 +92,18 @@ __device__ __forceinline__ void st_seg(float* p, const float* r) {
   }
 }
 
-// sum over the 8 lanes of a state row
+// sum over the 16 lanes of a row pair
 __device__ __forceinline__ float row_sum(float x) {
   x += __shfl_xor_sync(0xffffffffu, x, 1);
   x += __shfl_xor_sync(0xffffffffu, x, 2);
   x += __shfl_xor_sync(0xffffffffu, x, 4);
+  x += __shfl_xor_sync(0xffffffffu, x, 8);
   return x;
 }
 
-// sum over the four rows a warp holds (lanes with the same column segment)
-__device__ __forceinline__ float warp_rows_sum(float x) {
-  x += __shfl_xor_sync(0xffffffffu, x, 8);
-  x += __shfl_xor_sync(0xffffffffu, x, 16);
-  return x;
+// sum over the warp's two row pairs (lanes with the same columns)
+__device__ __forceinline__ float pair_sum(float x) {
+  return x + __shfl_xor_sync(0xffffffffu, x, 16);
 }
 
 template <typename T, typename Gt, int D>
@@ -115,6 +116,7 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
                float* __restrict__ scratch, int64_t L) {
   using C = BwdCfg<D>;
   constexpr int CPT = C::CPT, NT = C::NT, NW = C::NW, RED = C::RED, CH = kBwdChunk;
+  constexpr int S = kBwdSeg;
   extern __shared__ float bsm[];
   float* s_q = bsm;              // [CH][D] each, fp32
   float* s_k = s_q + CH * D;
@@ -124,7 +126,8 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   float* s_g = s_b + CH;         // [CH]
   float* s_red = s_g + CH;       // [2][NW][RED]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row = tid / kBwdTPR, seg = tid % kBwdTPR;  // columns seg + kBwdTPR * c
+  const int seg = tid % S;             // columns seg + S * c
+  const int r0 = 2 * (tid / S);        // rows r0 and r0 + 1
   const int64_t head = blockIdx.x;
   const int64_t nch = (L + CH - 1) / CH;
   const int64_t chs = L < CH ? L : CH;  // scratch states per head
@@ -135,14 +138,15 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   const T* doh = dout + head * L * D;
   float* ck = ckpt + head * nch * DD;
   float* sc = scratch + head * chs * DD;
-  // this thread's CPT values inside a [D, D] state: in the workspace (checkpoints,
-  // scratch) as one contiguous segment, read back only by this thread; in the
-  // caller's row-major h0, dhT and dh0 at row * D + seg + kBwdTPR * c
-  const int64_t my = (int64_t)row * D + seg * CPT;
-  const int64_t mine = (int64_t)row * D + seg;
-  auto ld_cols = [&](const float* p, float* r) {
+  // this thread's 2 * CPT values of a [D, D] state: in the workspace
+  // (checkpoints, scratch) one contiguous segment, read back only by this
+  // thread; in the caller's row-major h0, dhT and dh0 at (r0 + e) * D + seg + S c
+  const int64_t my = (int64_t)tid * (2 * CPT);
+  auto ld_cols = [&](const float* p, float (*r)[CPT]) {
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) r[c] = p[mine + kBwdTPR * c];
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) r[e][c] = p[(int64_t)(r0 + e) * D + seg + S * c];
   };
 
   // chunk c's inputs into shared memory as fp32; returns its step count
@@ -167,44 +171,58 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     return n;
   };
 
-  // one forward step of this thread's row segment
-  auto fwd_step = [&](float* h, int tl) {
+  // one forward step of this thread's two row segments
+  auto fwd_step = [&](float (*h)[CPT], int tl) {
     const float* kr = s_k + tl * D + seg;
-    float r = 0.f;
+    float kv[CPT];
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) r = fmaf(h[c], kr[kBwdTPR * c], r);
-    r = row_sum(r);
-    const float bu = s_b[tl] * (s_v[tl * D + row] - r);
-    const float gt = s_g[tl];
+    for (int c = 0; c < CPT; ++c) kv[c] = kr[S * c];
+    float r[2] = {0.f, 0.f};
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) h[c] = fmaf(gt, h[c], bu * kr[kBwdTPR * c]);
+    for (int c = 0; c < CPT; ++c) {
+      r[0] = fmaf(h[0][c], kv[c], r[0]);
+      r[1] = fmaf(h[1][c], kv[c], r[1]);
+    }
+    r[0] = row_sum(r[0]);
+    r[1] = row_sum(r[1]);
+    const float bt = s_b[tl], gt = s_g[tl];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float bu = bt * (s_v[tl * D + r0 + e] - r[e]);
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) h[e][c] = fmaf(gt, h[e][c], bu * kv[c]);
+    }
   };
 
   // ---- 1. forward: the state entering every chunk
   {
-    float h[CPT];
+    float h[2][CPT];
     if (h0) {
       ld_cols(h0 + head * DD, h);
     } else {
 #pragma unroll
-      for (int c = 0; c < CPT; ++c) h[c] = 0.f;
+      for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) h[e][c] = 0.f;
     }
     for (int64_t c = 0; c < nch; ++c) {
       __syncthreads();  // the previous chunk's staged rows are no longer read
       const int n = stage(c, false);
       __syncthreads();
-      st_seg<CPT>(ck + c * DD + my, h);
+      st_seg<2 * CPT>(ck + c * DD + my, &h[0][0]);
       for (int tl = 0; tl < n; ++tl) fwd_step(h, tl);
     }
   }
 
   // ---- 2. chunks in reverse
-  float G[CPT];
+  float G[2][CPT];
   if (dhT) {
     ld_cols(dhT + head * DD, G);
   } else {
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) G[c] = 0.f;
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) G[e][c] = 0.f;
   }
   int rb = 0;
   for (int64_t c = nch - 1; c >= 0; --c) {
@@ -214,55 +232,77 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     {
       // the chunk's states, recomputed from its checkpoint: scratch[tl] = the
       // state before step tl
-      float h[CPT];
-      ld_seg<CPT>(ck + c * DD + my, h);
+      float h[2][CPT];
+      ld_seg<2 * CPT>(ck + c * DD + my, &h[0][0]);
       for (int tl = 0; tl < n; ++tl) {
-        st_seg<CPT>(sc + tl * DD + my, h);
+        st_seg<2 * CPT>(sc + tl * DD + my, &h[0][0]);
         fwd_step(h, tl);
       }
     }
-    float hp[CPT];  // the state before step tl
-    ld_seg<CPT>(sc + (n - 1) * DD + my, hp);
+    float hp[2][CPT];  // the state before step tl
+    ld_seg<2 * CPT>(sc + (n - 1) * DD + my, &hp[0][0]);
     for (int tl = n - 1; tl >= 0; --tl) {
       const int64_t t = c * CH + tl;
       const float* kr = s_k + tl * D + seg;
       const float* qr = s_q + tl * D + seg;
-      const float do_i = s_do[tl * D + row];
-      const float bt = s_b[tl], gt = s_g[tl];
-      float gk = 0.f, hk = 0.f, gh = 0.f;
+      float kv[CPT], qv[CPT];
 #pragma unroll
       for (int cc = 0; cc < CPT; ++cc) {
-        G[cc] = fmaf(do_i, qr[kBwdTPR * cc], G[cc]);
-        gk = fmaf(G[cc], kr[kBwdTPR * cc], gk);
-        hk = fmaf(hp[cc], kr[kBwdTPR * cc], hk);
-        gh = fmaf(G[cc], hp[cc], gh);
+        kv[cc] = kr[S * cc];
+        qv[cc] = qr[S * cc];
       }
-      gk = row_sum(gk);
-      hk = row_sum(hk);
-      gh = row_sum(gh);
-      const float delta = s_v[tl * D + row] - hk;
-      if ((tid % kBwdTPR) == 0) dv[(head * L + t) * D + row] = from_f<T>(bt * gk);
+      const float bt = s_b[tl], gt = s_g[tl];
+      float do_r[2], gk[2], hk[2], gh[2], delta[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        do_r[e] = s_do[tl * D + r0 + e];
+        gk[e] = 0.f;
+        hk[e] = 0.f;
+        gh[e] = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < CPT; ++cc) {
+          G[e][cc] = fmaf(do_r[e], qv[cc], G[e][cc]);
+          gk[e] = fmaf(G[e][cc], kv[cc], gk[e]);
+          hk[e] = fmaf(hp[e][cc], kv[cc], hk[e]);
+          gh[e] = fmaf(G[e][cc], hp[e][cc], gh[e]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        gk[e] = row_sum(gk[e]);
+        hk[e] = row_sum(hk[e]);
+        gh[e] = row_sum(gh[e]);
+        delta[e] = s_v[tl * D + r0 + e] - hk[e];
+      }
+      if (seg == 0) {
+        dv[(head * L + t) * D + r0] = from_f<T>(bt * gk[0]);
+        dv[(head * L + t) * D + r0 + 1] = from_f<T>(bt * gk[1]);
+      }
       float* red = s_red + (rb * NW + warp) * RED;
 #pragma unroll
       for (int cc = 0; cc < CPT; ++cc) {
-        const float pq = warp_rows_sum(do_i * hp[cc]);
-        const float pk = warp_rows_sum(fmaf(G[cc], delta, -gk * hp[cc]));
-        if (lane < kBwdTPR) {
-          red[seg + kBwdTPR * cc] = pq;
-          red[D + seg + kBwdTPR * cc] = pk;
+        const float pq = pair_sum(fmaf(do_r[0], hp[0][cc], do_r[1] * hp[1][cc]));
+        const float pk = pair_sum(fmaf(G[0][cc], delta[0], -gk[0] * hp[0][cc]) +
+                                  fmaf(G[1][cc], delta[1], -gk[1] * hp[1][cc]));
+        if (lane < S) {
+          red[seg + S * cc] = pq;
+          red[D + seg + S * cc] = pk;
         }
       }
-      if (tl > 0) ld_seg<CPT>(sc + (tl - 1) * DD + my, hp);  // hp is dead from here on
-      const float s_gd = warp_rows_sum(gk * delta);
-      const float s_gh = warp_rows_sum(gh);
-      const float s_dd = warp_rows_sum(do_i * delta);
+      // hp is dead from here on: the next step's state loads during the sums
+      if (tl > 0) ld_seg<2 * CPT>(sc + (tl - 1) * DD + my, &hp[0][0]);
+      const float s_gd = pair_sum(fmaf(gk[0], delta[0], gk[1] * delta[1]));
+      const float s_gh = pair_sum(gh[0] + gh[1]);
+      const float s_dd = pair_sum(fmaf(do_r[0], delta[0], do_r[1] * delta[1]));
       if (lane == 0) {
         red[2 * D] = s_gd;
         red[2 * D + 1] = s_gh;
         red[2 * D + 2] = s_dd;
       }
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) G[cc] = fmaf(gt, G[cc], -bt * gk * kr[kBwdTPR * cc]);
+      for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int cc = 0; cc < CPT; ++cc) G[e][cc] = fmaf(gt, G[e][cc], -bt * gk[e] * kv[cc]);
       __syncthreads();
       // the step's sums over all rows, warps added in a fixed order
       const float* rr = s_red + rb * NW * RED;
@@ -275,26 +315,28 @@ gdr_bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
         }
         dq[(head * L + t) * D + tid] = from_f<T>(fmaf(gt, sq, bt * s_k[tl * D + tid] * sd));
       } else if (tid < 2 * D) {
-        float s = 0.f;
+        float sum = 0.f;
 #pragma unroll 4
-        for (int w = 0; w < NW; ++w) s += rr[w * RED + tid];
-        dk[(head * L + t) * D + (tid - D)] = from_f<T>(bt * s);
+        for (int w = 0; w < NW; ++w) sum += rr[w * RED + tid];
+        dk[(head * L + t) * D + (tid - D)] = from_f<T>(bt * sum);
       } else if (tid < 2 * D + 2) {
         const int which = tid - 2 * D;  // 0: dbeta, 1: dg
-        float s = 0.f;
+        float sum = 0.f;
 #pragma unroll 4
-        for (int w = 0; w < NW; ++w) s += rr[w * RED + 2 * D + which];
+        for (int w = 0; w < NW; ++w) sum += rr[w * RED + 2 * D + which];
         if (which == 0)
-          dbeta[head * L + t] = from_f<Gt>(s);
+          dbeta[head * L + t] = from_f<Gt>(sum);
         else
-          dg[head * L + t] = from_f<Gt>(s);
+          dg[head * L + t] = from_f<Gt>(sum);
       }
       rb ^= 1;
     }
   }
   if (dh0) {
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) dh0[head * DD + mine + kBwdTPR * c] = G[c];
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) dh0[head * DD + (int64_t)(r0 + e) * D + seg + S * c] = G[e][c];
   }
 }
 
