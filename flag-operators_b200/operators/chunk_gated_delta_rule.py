@@ -30,6 +30,7 @@ import ctypes
 import logging
 
 import torch
+from torch.autograd.function import once_differentiable
 
 from . import _lib
 
@@ -97,7 +98,10 @@ class _GatedDeltaRule(torch.autograd.Function):
         return o
 
     @staticmethod
+    @once_differentiable
     def backward(ctx, do, dhT=None):
+        # first derivatives only: a double backward raises instead of returning
+        # wrong second derivatives
         q, k, v, beta, g, h0 = ctx.saved_tensors
         dq, dk, dv, dbeta, dg, dh0 = _backward(q, k, v, beta, g, h0, do, dhT,
                                                h0 is not None and ctx.needs_input_grad[5])
