@@ -26,6 +26,7 @@ from .ops import (  # noqa: F401
     delta_rule_forward,
     delta_rule_grads,
     delta_rule_backward,
+    delta_rule_backward_chunked,
     ce_shard_stats,
     ce_shard_combine,
     ce_rows_partial,

@@ -265,6 +265,102 @@ def delta_rule_backward(q, k, v, beta, g, do, initial_state=None, dhT=None):
     return {"q": dq, "k": dk, "v": dv, "beta": dbeta, "g": dg, "initial_state": G}
 
 
+def delta_rule_backward_chunked(q, k, v, beta, g, do, initial_state=None, dhT=None, C=16):
+    """The chunked backward (the form a tensor-core kernel would take), float64.
+
+    Forward of a chunk with entry state S [Dv, Dk], tokens t = 0..n-1, in-chunk
+    gate products gam_t = g_0 ... g_t (gam_{-1} = 1), ratio(t, s) = gam_t / gam_s:
+      A[t,s] = ratio(t-1,s) beta_s k_t.k_s (s < t),  T = (I + A)^-1
+      R = V - diag(gam_{t-1}) K S^T,  U = T R
+      P[t,s] = ratio(t,s) beta_s q_t.k_s (s <= t),  O = diag(gam_t) Q S^T + P U
+      Kt[s] = ratio(n-1,s) beta_s k_s,  S' = gam_{n-1} S + U^T Kt
+    Backward of the chunk, given dO and dS' (the transposes of those products):
+      dU = P^T dO + Kt dS'^T;  dP = dO U^T (s <= t);  dKt = U dS'
+      dR = T^T dU;  dT = dU R^T;  dA = -T^T dT T^T (s < t);  dV = dR
+      dS = dO^T diag(gam) Q + gam_{n-1} dS' - dR^T diag(gam_{t-1}) K
+      dQ = diag(gam) dO S + (dP o ratio o beta) K
+      dK = -diag(gam_{t-1}) dR S + (dA o ratio' o beta) K + (dA o ratio' o beta)^T K
+           + (dP o ratio o beta)^T Q + diag(ratio(n-1,.) beta) dKt
+    and dbeta, dgam from the same products; dg_r = sum_{t >= r} dgam_t gam_t / g_r
+    inside the chunk.  dS is carried to the previous chunk as its dS'.  Gates must
+    be nonzero (the ratios are formed by division).  Checked against
+    delta_rule_grads (autograd) by the CPU tests.
+    """
+    q, k, v, beta, g, do = (_cpu(t).double() for t in (q, k, v, beta, g, do))
+    B, H, L, D = q.shape
+    S = (torch.zeros(B, H, D, D, dtype=torch.float64) if initial_state is None
+         else _cpu(initial_state).double().clone())
+    nch = (L + C - 1) // C
+    entry = []
+    chunks = []
+    for c in range(nch):
+        t0, t1 = c * C, min(L, (c + 1) * C)
+        Q, K, V = q[:, :, t0:t1], k[:, :, t0:t1], v[:, :, t0:t1]
+        bt, gt = beta[:, :, t0:t1], g[:, :, t0:t1]
+        n = t1 - t0
+        gam = torch.cumprod(gt, dim=-1)                                   # [B,H,n]
+        gm1 = torch.cat([torch.ones_like(gam[..., :1]), gam[..., :-1]], -1)
+        low = torch.tril(torch.ones(n, n, dtype=torch.float64), -1)
+        lowd = torch.tril(torch.ones(n, n, dtype=torch.float64))
+        rA = gm1[..., :, None] / gam[..., None, :]                        # ratio(t-1, s)
+        rP = gam[..., :, None] / gam[..., None, :]                        # ratio(t, s)
+        A = low * rA * bt[..., None, :] * (K @ K.transpose(-1, -2))
+        T = torch.linalg.inv(torch.eye(n, dtype=torch.float64) + A)
+        R = V - gm1[..., None] * (K @ S.transpose(-1, -2))
+        U = T @ R
+        P = lowd * rP * bt[..., None, :] * (Q @ K.transpose(-1, -2))
+        rK = gam[..., -1:] / gam                                          # ratio(n-1, s)
+        Kt = (rK * bt)[..., None] * K
+        entry.append(S)
+        chunks.append((t0, t1, Q, K, V, bt, gt, gam, gm1, low, lowd, rA, rP, T, R, U, P, rK, Kt))
+        S = gam[..., -1, None, None] * S + U.transpose(-1, -2) @ Kt
+    dS_next = (torch.zeros(B, H, D, D, dtype=torch.float64) if dhT is None
+               else _cpu(dhT).double().clone())
+    dq, dk, dv = torch.zeros_like(q), torch.zeros_like(k), torch.zeros_like(v)
+    dbeta, dg = torch.zeros_like(beta), torch.zeros_like(g)
+    for c in reversed(range(nch)):
+        (t0, t1, Q, K, V, bt, gt, gam, gm1, low, lowd, rA, rP, T, R, U, P, rK, Kt) = chunks[c]
+        S = entry[c]
+        dO = do[:, :, t0:t1]
+        Sk = K @ S.transpose(-1, -2)                                      # rows S k_t
+        Sq = Q @ S.transpose(-1, -2)                                      # rows S q_t
+        dU = P.transpose(-1, -2) @ dO + Kt @ dS_next.transpose(-1, -2)
+        dP = lowd * (dO @ U.transpose(-1, -2))
+        dKt = U @ dS_next
+        dR = T.transpose(-1, -2) @ dU
+        dT = dU @ R.transpose(-1, -2)
+        dA = low * -(T.transpose(-1, -2) @ dT @ T.transpose(-1, -2))
+        dS = (dO.transpose(-1, -2) @ (gam[..., None] * Q) + gam[..., -1, None, None] * dS_next
+              - dR.transpose(-1, -2) @ (gm1[..., None] * K))
+        MP = dP * rP * bt[..., None, :]
+        MA = dA * rA * bt[..., None, :]
+        dq[:, :, t0:t1] = gam[..., None] * (dO @ S) + MP @ K
+        dk[:, :, t0:t1] = (-gm1[..., None] * (dR @ S) + MA @ K + MA.transpose(-1, -2) @ K
+                           + MP.transpose(-1, -2) @ Q + (rK * bt)[..., None] * dKt)
+        dv[:, :, t0:t1] = dR
+        KK, QK = K @ K.transpose(-1, -2), Q @ K.transpose(-1, -2)
+        dbeta[:, :, t0:t1] = ((dA * rA * KK).sum(-2) + (dP * rP * QK).sum(-2)
+                              + rK * (dKt * K).sum(-1))
+        # gradients with respect to the in-chunk gate products gam
+        GA = dA * bt[..., None, :] * KK                                   # d/d ratio(t-1, s)
+        GP = dP * bt[..., None, :] * QK                                   # d/d ratio(t, s)
+        GK = bt * (dKt * K).sum(-1)                                       # d/d ratio(n-1, s)
+        dgam = (dO * Sq).sum(-1)                                          # O direct term
+        dgam = dgam + (GP / gam[..., None, :]).sum(-1)
+        dgam = dgam - (GP * gam[..., :, None]).sum(-2) / gam ** 2
+        dgam = dgam - (GA * gm1[..., :, None]).sum(-2) / gam ** 2
+        dgm1 = (GA / gam[..., None, :]).sum(-1) - (dR * Sk).sum(-1)       # d/d gam_{t-1}
+        dgam[..., :-1] = dgam[..., :-1] + dgm1[..., 1:]
+        dgam[..., -1] = (dgam[..., -1] + (dS_next * S).sum((-1, -2))
+                         + (GK / gam).sum(-1))
+        dgam = dgam - GK * gam[..., -1:] / gam ** 2
+        # gam_t = g_0 ... g_t: dg_r = sum_{t >= r} dgam_t gam_t / g_r
+        suffix = torch.flip(torch.cumsum(torch.flip(dgam * gam, [-1]), -1), [-1])
+        dg[:, :, t0:t1] = suffix / gt
+        dS_next = dS
+    return {"q": dq, "k": dk, "v": dv, "beta": dbeta, "g": dg, "initial_state": dS_next}
+
+
 # ---------------------------------------------------------------------------
 # vocabulary-sharded cross-entropy: statement of the sharded algorithm on CPU
 # (used by the multi-process tests to check the host logic and the combine rule;

@@ -187,3 +187,25 @@ def test_delta_rule_backward_restatement_matches_autograd(with_h0, with_dhT):
         r = r.double()
         scale = r.abs().max().item()
         assert (got[name] - r).abs().max().item() <= 1e-5 * scale + 1e-12, name
+
+
+@pytest.mark.parametrize("C", [1, 5, 16, 64])
+@pytest.mark.parametrize("with_state", [False, True])
+def test_delta_rule_chunked_backward_algebra_matches_autograd(C, with_state):
+    """The chunked backward (per chunk: transposes of T, U, P, Kt and the state
+    products, gate gradients through the in-chunk products) equals autograd
+    through the reference's loop for any chunk size, ragged last chunk included."""
+    gen = torch.Generator().manual_seed(11)
+    B, H, L, D = 2, 2, 37, 8
+    q, k, v, do = (torch.randn(B, H, L, D, generator=gen, dtype=torch.float64)
+                   for _ in range(4))
+    k = k / k.norm(dim=-1, keepdim=True)
+    beta = torch.sigmoid(torch.randn(B, H, L, generator=gen, dtype=torch.float64))
+    g = 0.5 + 0.5 * torch.sigmoid(torch.randn(B, H, L, generator=gen, dtype=torch.float64))
+    h0 = torch.randn(B, H, D, D, generator=gen, dtype=torch.float64) if with_state else None
+    dhT = torch.randn(B, H, D, D, generator=gen, dtype=torch.float64) if with_state else None
+    ref = oracle.delta_rule_grads(q, k, v, beta, g, do, h0, dhT)
+    got = oracle.delta_rule_backward_chunked(q, k, v, beta, g, do, h0, dhT, C=C)
+    for name, r in ref.items():
+        r = r.double()
+        assert (got[name] - r).abs().max().item() <= 1e-5 * r.abs().max().item(), name
